@@ -1,0 +1,216 @@
+"""CPU oracle -- TEST INFRASTRUCTURE ONLY.
+
+numpy front end of oracle/rlscan_oracle.c (the C restatement of the
+reference's sequential estimators).  Only tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline / reference arm import this module; the rl_triton
+package never does.
+
+Every function takes numpy float32 arrays (int64 for Retrace actions) and
+returns float32 or float64 arrays (`precision="f32"` reproduces the
+reference's fp32 sequential loops, `"f64"` is the higher-precision yardstick).
+Rows are split over a thread pool; each ctypes call releases the GIL.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc only)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def _load():
+    if not os.path.exists(LIB_PATH):
+        build()
+    return ctypes.CDLL(LIB_PATH)
+
+
+_lib = _load()
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_D = ctypes.c_double
+_I = ctypes.c_int
+
+_ARGS = {
+    "orc_gae": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _D, _D],
+    "orc_vtrace": [_P, _P, _P, _P, _P, _P, _P, _I, _P, _P, _I64, _I64, _D, _D, _D],
+    "orc_retrace": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _D, _D, _D, _D],
+    "orc_lambda": [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _D, _D],
+    "orc_discounted": [_P, _P, _P, _P, _I, _P, _I64, _I64, _D],
+    "orc_eligibility": [_P, _P, _P, _P, _I64, _I64, _D, _D],
+    "orc_prefix": [_P, _P, _P, _I, _P, _I64, _I64],
+    "orc_scan": [_P, _P, _P, _I, _P, _I64, _I64],
+}
+for _n, _a in _ARGS.items():
+    for _s in ("_f32", "_f64"):
+        f = getattr(_lib, _n + _s)
+        f.argtypes = _a
+        f.restype = None
+
+BOOT_NONE, BOOT_ROW, BOOT_LASTCOL, BOOT_FULL_ADD, BOOT_FULL_SEL = range(5)
+
+_THREADS = int(os.environ.get("RLS_ORACLE_THREADS", os.cpu_count() or 1))
+
+
+def threads() -> int:
+    return _THREADS
+
+
+def _f32(a):
+    if a is None:
+        return None
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a, off=0):
+    if a is None:
+        return None
+    return a.ctypes.data + off * a.itemsize
+
+
+def _rows(N: int, fn, nthreads: int | None = None) -> None:
+    """Run fn(row_start, row_count) over row blocks on a thread pool."""
+    nt = max(1, min(nthreads or _THREADS, N))
+    if nt == 1:
+        fn(0, N)
+        return
+    bounds = np.linspace(0, N, nt + 1).astype(np.int64)
+    with ThreadPoolExecutor(nt) as ex:
+        list(ex.map(lambda k: fn(int(bounds[k]), int(bounds[k + 1] - bounds[k])), range(nt)))
+
+
+def _out(shape, precision):
+    return np.empty(shape, dtype=np.float32 if precision == "f32" else np.float64)
+
+
+def gae(r, v, term, trunc=None, boot=None, kind=BOOT_NONE, gamma=0.99, lam=0.95, precision="f32", nthreads=None):
+    r, v, term, trunc, boot = map(_f32, (r, v, term, trunc, boot))
+    N, T = r.shape
+    out = _out((N, T), precision)
+    fn = getattr(_lib, "orc_gae_" + precision)
+    row_boot = kind == BOOT_ROW
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(r, o), _p(v, o), _p(term, o), _p(trunc, o), _p(boot, n0 if row_boot else o), kind,
+           _p(out, o), cnt, T, gamma, lam)
+
+    _rows(N, go, nthreads)
+    return out
+
+
+def vtrace(lpt, lpb, v, r, term, trunc=None, boot=None, kind=BOOT_NONE, gamma=0.99, rho_bar=1.0, c_bar=1.0,
+           precision="f32", nthreads=None):
+    lpt, lpb, v, r, term, trunc, boot = map(_f32, (lpt, lpb, v, r, term, trunc, boot))
+    N, T = r.shape
+    vs, adv = _out((N, T), precision), _out((N, T), precision)
+    fn = getattr(_lib, "orc_vtrace_" + precision)
+    row_boot = kind == BOOT_ROW
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(lpt, o), _p(lpb, o), _p(v, o), _p(r, o), _p(term, o), _p(trunc, o),
+           _p(boot, n0 if row_boot else o), kind, _p(vs, o), _p(adv, o), cnt, T, gamma, rho_bar, c_bar)
+
+    _rows(N, go, nthreads)
+    return vs, adv
+
+
+def retrace(pi, mu, q, nq, act, r, term, trunc, gamma=0.99, lam=1.0, c_bar=1.0, rho_bar=1.0, precision="f32",
+            nthreads=None):
+    pi, mu, q, nq, r, term, trunc = map(_f32, (pi, mu, q, nq, r, term, trunc))
+    act = np.ascontiguousarray(act, dtype=np.int64)
+    N, T = r.shape
+    A = pi.shape[2]
+    qret, adv = _out((N, T), precision), _out((N, T), precision)
+    fn = getattr(_lib, "orc_retrace_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(pi, o * A), _p(mu, o), _p(q, o), _p(nq, o * A), _p(act, o), _p(r, o), _p(term, o), _p(trunc, o),
+           _p(qret, o), _p(adv, o), cnt, T, A, gamma, lam, c_bar, rho_bar)
+
+    _rows(N, go, nthreads)
+    return qret, adv
+
+
+def lambda_returns(r, nv, term, trunc=None, boot=None, kind=BOOT_NONE, gamma=0.99, lam=0.95, precision="f32",
+                   nthreads=None):
+    r, nv, term, trunc, boot = map(_f32, (r, nv, term, trunc, boot))
+    N, T = r.shape
+    out = _out((N, T), precision)
+    fn = getattr(_lib, "orc_lambda_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(r, o), _p(nv, o), _p(term, o), _p(trunc, o), _p(boot, o), kind, _p(out, o), cnt, T, gamma, lam)
+
+    _rows(N, go, nthreads)
+    return out
+
+
+def discounted_returns(r, term, trunc=None, boot=None, kind=BOOT_NONE, gamma=0.99, precision="f32",
+                       nthreads=None):
+    r, term, trunc, boot = map(_f32, (r, term, trunc, boot))
+    N, T = r.shape
+    out = _out((N, T), precision)
+    fn = getattr(_lib, "orc_discounted_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(r, o), _p(term, o), _p(trunc, o), _p(boot, o), kind, _p(out, o), cnt, T, gamma)
+
+    _rows(N, go, nthreads)
+    return out
+
+
+def eligibility_traces(g, dones, gamma, lam, seed=None, precision="f32", nthreads=None):
+    g, dones, seed = map(_f32, (g, dones, seed))
+    N, T = g.shape
+    out = _out((N, T), precision)
+    fn = getattr(_lib, "orc_eligibility_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(g, o), _p(dones, o), _p(seed, n0), _p(out, o), cnt, T, gamma, lam)
+
+    _rows(N, go, nthreads)
+    return out
+
+
+def prefix_sum(x, dones, seed=None, ends_at=True, precision="f32", nthreads=None):
+    x, dones, seed = map(_f32, (x, dones, seed))
+    N, T = x.shape
+    out = _out((N, T), precision)
+    fn = getattr(_lib, "orc_prefix_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(x, o), _p(dones, o), _p(seed, n0), 1 if ends_at else 0, _p(out, o), cnt, T)
+
+    _rows(N, go, nthreads)
+    return out
+
+
+def affine_scan(u, v, carry=None, direction=0, precision="f32", nthreads=None):
+    u, v, carry = map(_f32, (u, v, carry))
+    N, T = u.shape
+    out = _out((N, T), precision)
+    fn = getattr(_lib, "orc_scan_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(u, o), _p(v, o), _p(carry, n0), direction, _p(out, o), cnt, T)
+
+    _rows(N, go, nthreads)
+    return out

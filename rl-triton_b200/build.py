@@ -1,0 +1,77 @@
+"""Build librlscan.so (sm_100a) in-tree.
+
+    python rl-triton_b200/build.py [--verbose]
+
+Compiles csrc/*.cu with nvcc for sm_100a only and writes
+rl_triton/_lib/librlscan.so next to the Python package, so the library
+travels with the source tree.  The C ABI is declared in include/rlscan.h.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+CSRC = os.path.join(HERE, "csrc")
+LIBDIR = os.path.join(HERE, "rl_triton", "_lib")
+LIB = os.path.join(LIBDIR, "librlscan.so")
+SOURCES = ["rlscan.cu", "segment.cu"]
+HEADERS = ["common.cuh", "algs.cuh", "scan_kernel.cuh"]
+
+
+def nvcc_path() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found; librlscan.so needs the CUDA toolkit to build")
+    return cand
+
+
+def nvcc_flags(verbose: bool = False) -> list[str]:
+    flags = [
+        "-gencode", "arch=compute_100a,code=sm_100a",
+        "-O3", "-lineinfo", "-std=c++17",
+        "-Xcompiler", "-fPIC", "-Xcompiler", "-O3",
+        "-I", os.path.join(ROOT, "include"),
+        "-I", CSRC,
+    ]
+    if verbose:
+        flags += ["-Xptxas", "-v"]
+    return flags
+
+
+def _stale() -> bool:
+    if not os.path.exists(LIB):
+        return True
+    t = os.path.getmtime(LIB)
+    deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
+    deps.append(os.path.join(ROOT, "include", "rlscan.h"))
+    return any(os.path.getmtime(d) > t for d in deps)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and not _stale():
+        return LIB
+    os.makedirs(LIBDIR, exist_ok=True)
+    tmp = LIB + ".tmp"
+    cmd = [nvcc_path(), *nvcc_flags(verbose), "-shared", "-o", tmp]
+    cmd += [os.path.join(CSRC, f) for f in SOURCES]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("nvcc failed building librlscan.so")
+    if verbose:
+        sys.stderr.write(res.stderr)
+    os.replace(tmp, LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill report")
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force or a.verbose, verbose=a.verbose))
