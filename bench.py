@@ -519,6 +519,18 @@ def run_b200(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_ncu(args, local):
+    cfg = CONFIGS[args.config]
+    dev = torch.device("cuda", local)
+    x = make_inputs(cfg, dev, seed=1)
+    calls = make_calls(cfg, x)
+    torch.cuda.synchronize(dev)
+    for _ in range(args.warmup + args.steps):
+        for f in calls.values():
+            f()
+    torch.cuda.synchronize(dev)
+
+
 def _used(key, cfg):
     fs = cfg["funcs"]
     need = {"r", "term"}
@@ -546,6 +558,10 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ncu", action="store_true",
+                    help="profiling mode for ncu: W warm-up rounds then K rounds of one eager launch per "
+                         "function, in --config order; no timing, no graphs, prints nothing")
+    ap.add_argument("--only", default="", help="comma list of functions to run (default: all of the config)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -553,8 +569,14 @@ def main():
         # CPU arm: no process group; under torchrun rank 0 alone runs and prints.
         run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
         return
+    if args.only:
+        for name in CONFIGS:
+            CONFIGS[name] = dict(CONFIGS[name], funcs=[f for f in CONFIGS[name]["funcs"] if f in args.only.split(",")])
     world, rank, local = dist_setup()
     try:
+        if args.ncu:
+            run_ncu(args, local)
+            return
         run_b200(args, world, rank, local)
     finally:
         if world > 1:

@@ -54,8 +54,10 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   const size_t smem = (size_t)g.smem_per_warp * kWarps;
   auto kern = scan_kernel<Alg, kWarps, R>;
-  if (smem > 48 * 1024) {
-    static thread_local int configured = 0;  // one attribute call per instantiation and thread
+  if (smem > 0) {
+    // Opt in to more than the default 48 KB (dynamic + static) once per
+    // instantiation and thread.
+    static thread_local int configured = 0;
     if (!configured) {
       if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess)
         return RLS_ECUDA;
@@ -150,6 +152,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
             const void* bootstrap, int boot_kind, float* advantages, int64_t num_envs, int64_t seq_len,
             float gamma, float lambda_, int in_dtype, const rls_segment_t* seg, void* ws, size_t ws_bytes,
             void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!rewards || !values || !terminateds || !advantages || !valid_dtype(in_dtype)) return RLS_EINVAL;
   if (boot_kind < RLS_BOOT_NONE || boot_kind > RLS_BOOT_FULL_SEL) return RLS_EINVAL;
   if ((boot_kind == RLS_BOOT_ROW || boot_kind == RLS_BOOT_LASTCOL) && !bootstrap) return RLS_EINVAL;
@@ -184,6 +187,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
                const void* terminateds, const void* truncateds, const void* bootstrap, int boot_kind,
                float* targets, float* advantages, int64_t num_envs, int64_t seq_len, float gamma, float rho_bar,
                float c_bar, int in_dtype, void* ws, size_t ws_bytes, void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!log_pi_target || !log_pi_behavior || !values || !rewards || !terminateds || !targets || !advantages ||
       !valid_dtype(in_dtype))
     return RLS_EINVAL;
@@ -220,6 +224,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
                 const float* terminateds, const float* truncateds, float* targets, float* advantages,
                 int64_t num_envs, int64_t seq_len, int64_t num_actions, float gamma, float lambda_, float c_bar,
                 float rho_bar, void* ws, size_t ws_bytes, void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!action_probs_target || !action_probs_behavior || !q_values || !next_q_values_all || !actions ||
       !rewards || !terminateds || !truncateds || !targets || !advantages || num_actions <= 0)
     return RLS_EINVAL;
@@ -258,6 +263,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
                        const void* truncateds, const void* bootstrap, int boot_kind, float* out, int64_t num_envs,
                        int64_t seq_len, float gamma, float lambda_, int in_dtype, const rls_segment_t* seg,
                        void* ws, size_t ws_bytes, void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!rewards || !next_values || !terminateds || !out || !valid_dtype(in_dtype)) return RLS_EINVAL;
   if (!(boot_kind == RLS_BOOT_NONE || boot_kind == RLS_BOOT_LASTCOL || boot_kind == RLS_BOOT_FULL_ADD))
     return RLS_EINVAL;
@@ -288,6 +294,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
                            const void* bootstrap, int boot_kind, float* out, int64_t num_envs, int64_t seq_len,
                            float gamma, int in_dtype, const rls_segment_t* seg, void* ws, size_t ws_bytes,
                            void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!rewards || !terminateds || !out || !valid_dtype(in_dtype)) return RLS_EINVAL;
   if (!(boot_kind == RLS_BOOT_NONE || boot_kind == RLS_BOOT_LASTCOL || boot_kind == RLS_BOOT_FULL_ADD))
     return RLS_EINVAL;
@@ -316,6 +323,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
 static int forward_common(const void* x, const void* dones, const float* seed, float* out, int64_t num_envs,
                           int64_t seq_len, float k, int prev, int in_dtype, const rls_segment_t* seg, void* ws,
                           size_t ws_bytes, void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!x || !dones || !out || !valid_dtype(in_dtype)) return RLS_EINVAL;
   if (seg && prev && seg->t0 > 0 && !seg->halo) return RLS_EINVAL;
   if (!aligned16(x) || !aligned16(dones) || !aligned16(out)) return RLS_EALIGN;
@@ -354,6 +362,7 @@ int rls_prefix_sum(const void* inputs, const void* dones, const float* seed_valu
 int rls_affine_scan(const float* u, const float* v, const float* carry, int direction, float* out,
                     int64_t num_envs, int64_t seq_len, const rls_segment_t* seg, void* ws, size_t ws_bytes,
                     void* stream) {
+  if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!u || !v || !out || (direction != 0 && direction != 1)) return RLS_EINVAL;
   if (!aligned16(u) || !aligned16(v) || !aligned16(out)) return RLS_EALIGN;
   Geom g;
