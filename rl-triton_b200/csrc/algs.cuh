@@ -35,6 +35,7 @@ struct Geom {
   int64_t S;          // local row length
   int64_t N;          // rows
   int64_t num_tiles;  // tiles of the launch
+  int64_t ws_cap;     // tiles the workspace can describe (its layout key)
   int edge_global;    // 1: local row edges are global row edges (no time split)
   int seg;            // 1: time-split launch (halo neighbours at cuts)
   int smem_per_warp;  // dynamic shared memory per warp (Retrace staging)
@@ -402,6 +403,29 @@ struct RetraceAlg {
       const float4 pv = *reinterpret_cast<const float4*>(pa_s + local);
       x.e[0] = ev.x; x.e[1] = ev.y; x.e[2] = ev.z; x.e[3] = ev.w;
       x.pa[0] = pv.x; x.pa[1] = pv.y; x.pa[2] = pv.z; x.pa[3] = pv.w;
+    } else if (p.A == 4 && full) {
+      // Row-kernel path, A = 4: one 16-byte vector per element of pi and Qn,
+      // the four int64 actions as two 16-byte vectors.
+      const longlong2 a01 = __ldcs(reinterpret_cast<const longlong2*>(p.act + i));
+      const longlong2 a23 = __ldcs(reinterpret_cast<const longlong2*>(p.act + i + 2));
+      const int64_t acts[4] = {a01.x, a01.y, a23.x, a23.y};
+#pragma unroll
+      for (int k = 0; k < kVec; ++k) {
+        const float4 pv = __ldcs(reinterpret_cast<const float4*>(p.pi + (i + k) * 4));
+        const float4 qv = __ldcs(reinterpret_cast<const float4*>(p.nq + (i + k) * 4));
+        float e = pv.x * qv.x;
+        e = fmaf(pv.y, qv.y, e);
+        e = fmaf(pv.z, qv.z, e);
+        e = fmaf(pv.w, qv.w, e);
+        const int64_t a = acts[k];
+        float pa = 0.f;
+        pa = (a == 0) ? pv.x : pa;
+        pa = (a == 1) ? pv.y : pa;
+        pa = (a == 2) ? pv.z : pa;
+        pa = (a == 3) ? pv.w : pa;
+        x.e[k] = e;
+        x.pa[k] = pa;
+      }
     } else {
 #pragma unroll
       for (int k = 0; k < kVec; ++k) {

@@ -69,14 +69,25 @@ __host__ __device__ inline size_t ws_bytes_for_tiles(int64_t ntiles) {
   return 64 + f + (size_t)ntiles * 16;
 }
 
-__host__ __device__ inline Workspace ws_carve(void* base, int64_t ntiles) {
+// Tiles a workspace of `bytes` can describe.  The layout is carved by this
+// capacity -- a property of the buffer, not of the launch -- so every launch on
+// one buffer sees the flags, aggregates and inclusive values at the same
+// places, and a stale aggregate can never be read as another launch's flag.
+__host__ __device__ inline int64_t ws_capacity(size_t bytes) {
+  if (bytes < 64 + 16 + 20) return 0;
+  int64_t cap = (int64_t)((bytes - 64 - 16) / 20);
+  while (cap > 0 && ws_bytes_for_tiles(cap) > bytes) --cap;
+  return cap;
+}
+
+__host__ __device__ inline Workspace ws_carve(void* base, int64_t capacity) {
   char* p = (char*)base;
   Workspace w;
   w.hdr = (WsHeader*)p;
   w.flags = (unsigned*)(p + 64);
-  size_t f = ((size_t)ntiles * 4 + 15) & ~(size_t)15;
+  size_t f = ((size_t)capacity * 4 + 15) & ~(size_t)15;
   w.agg = (float2*)(p + 64 + f);
-  w.incl = w.agg + ntiles;
+  w.incl = w.agg + capacity;
   return w;
 }
 

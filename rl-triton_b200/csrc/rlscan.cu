@@ -6,9 +6,12 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 
 #include "rlscan.h"
 #include "scan_kernel.cuh"
+#include "rows_kernel.cuh"
+#include "tile_policies.cuh"
 
 using namespace rls;
 
@@ -50,8 +53,9 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
   constexpr int64_t tile = (int64_t)kWarps * R * 32 * Alg::kVec;
   g.num_tiles = (g.M + tile - 1) / tile;
   if (g.num_tiles == 0) return RLS_OK;
-  if (!ws || ws_bytes < ws_bytes_for_tiles(g.num_tiles)) return RLS_EWORKSPACE;
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
+  g.ws_cap = ws ? ws_capacity(ws_bytes) : 0;
+  if (g.ws_cap < g.num_tiles) return RLS_EWORKSPACE;
   const size_t smem = (size_t)g.smem_per_warp * kWarps;
   auto kern = scan_kernel<Alg, kWarps, R>;
   if (smem > 0) {
@@ -68,9 +72,200 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
 }
 
+// ---- row-parallel path ------------------------------------------------
+constexpr int kRowWarps = 4;  // rows (warps) per CTA of the row kernel
+
+int env_int(const char* name, int dflt) {
+  const char* s = std::getenv(name);
+  return s ? std::atoi(s) : dflt;
+}
+
+// The row kernel needs every row to start on a 16-byte boundary; other shapes
+// fall back to the flat look-back kernel.
+template <class Alg>
+bool use_rows(const Geom& g) {
+  return g.S % Alg::kVec == 0;
+}
+
+template <class Alg, int R>
+int launch_rows_r(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
+  const int64_t blocks = (g.N + kRowWarps - 1) / kRowWarps;
+  if (blocks > 0x7fffffffLL) return RLS_EINVAL;
+  rows_kernel<Alg, kRowWarps, R><<<(unsigned)blocks, kRowWarps * 32, 0, s>>>(p, g);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+}
+
+// Rounds per chunk: enough 16-byte vectors in flight per lane without
+// padding short rows (a 128-step fp32 row is exactly one round).
+template <class Alg, int MAXR>
+int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
+  const int forced = env_int("RLS_ROWS_ROUNDS", 0);
+  const int64_t run = 32 * Alg::kVec;
+  int r = forced ? forced : (int)std::min<int64_t>((g.S + run - 1) / run, MAXR);
+  if (r >= 4 && MAXR >= 4) return launch_rows_r<Alg, (MAXR >= 4 ? 4 : 1)>(p, g, s);
+  if (r >= 2 && MAXR >= 2) return launch_rows_r<Alg, (MAXR >= 2 ? 2 : 1)>(p, g, s);
+  return launch_rows_r<Alg, 1>(p, g, s);
+}
+
+// ---- TMA-staged tile path (default) ----------------------------------------
+// Which kernel family serves a call: RLS_PATH=tile (default) | rows | flat.
+// rows/flat are the register-only kernels, kept as cross-checks.
+int path_mode() {
+  const char* s = std::getenv("RLS_PATH");
+  if (!s || !*s) return 0;
+  if (!std::strcmp(s, "rows")) return 1;
+  if (!std::strcmp(s, "flat")) return 2;
+  return 0;
+}
+
+int num_sms(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+template <class P, int K>
+int launch_tile_k(const typename P::Params& p, TileGeom tg, void* ws, size_t ws_bytes, cudaStream_t s) {
+  constexpr int64_t TILE = (int64_t)kTileThreads * K;
+  tg.num_tiles = (tg.M + TILE - 1) / TILE;
+  if (tg.num_tiles == 0) return RLS_OK;
+  if (tg.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
+  tg.ws_cap = ws ? ws_capacity(ws_bytes) : 0;
+  if (tg.ws_cap < tg.num_tiles) return RLS_EWORKSPACE;
+  const size_t smem = (size_t)tg.stages * tg.stage_bytes + (size_t)TILE * 4 * (P::kOutSlots + P::kScratch);
+  auto kern = tile_kernel<P, K>;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
+  // Per-device opt-in to large dynamic shared memory, and the resident CTAs
+  // per SM for the smem size last used (occupancy is a host-side query).
+  static unsigned long long configured = 0;
+  static size_t occ_smem[64] = {0};
+  static int occ_val[64] = {0};
+  if (dev < 64 && !(configured & (1ull << dev))) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024) != cudaSuccess)
+      return RLS_ECUDA;
+    configured |= 1ull << dev;
+  }
+  int per_sm = 1;
+  if (dev < 64 && occ_smem[dev] == smem && occ_val[dev] > 0) {
+    per_sm = occ_val[dev];
+  } else {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kTileThreads, smem) != cudaSuccess ||
+        per_sm <= 0)
+      return RLS_ECUDA;
+    if (dev < 64) { occ_smem[dev] = smem; occ_val[dev] = per_sm; }
+  }
+  const int cap_env = env_int("RLS_TILE_CTAS_PER_SM", 0);
+  if (cap_env > 0 && cap_env < per_sm) per_sm = cap_env;
+  int64_t grid = (int64_t)per_sm * num_sms(dev);
+  if (grid > tg.num_tiles) grid = tg.num_tiles;
+  // Cooperative launch: the round-robin tile order needs all CTAs resident.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kTileThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, p, tg, ws) != cudaSuccess) return RLS_ECUDA;
+  return RLS_OK;
+}
+
+// Stage layout: every staged stream gets a 128-byte-aligned slot of TILE*esz
+// bytes; returns the stage size.
+template <class P>
+int stage_layout(const typename P::Params& p, int K, int* off) {
+  const int64_t tile = (int64_t)kTileThreads * K;
+  int64_t cur = 0;
+  for (int k = 0; k < kMaxStreams; ++k) off[k] = 0;
+  for (int k = 0; k < P::kNS; ++k) {
+    off[k] = (int)cur;
+    cur += (tile * P::esz(p, k) + 127) & ~(int64_t)127;
+  }
+  return (int)cur;
+}
+
+// Ring depth: the deepest ring (4..2 stages) within the per-CTA budget, which
+// by default leaves room for two CTAs per SM.
+template <class P, int K>
+int launch_tile(const typename P::Params& p, const Geom& g, void* ws, size_t ws_bytes, cudaStream_t s) {
+  if (g.M == 0) return RLS_OK;
+  TileGeom tg;
+  tg.M = g.M; tg.S = g.S; tg.N = g.N; tg.num_tiles = 0; tg.ws_cap = 0;
+  tg.edge_global = g.edge_global; tg.seg = g.seg;
+  tg.stage_bytes = stage_layout<P>(p, K, tg.off);
+  const int64_t outb = (int64_t)kTileThreads * K * 4 * (P::kOutSlots + P::kScratch);
+  const int64_t budget = (int64_t)env_int("RLS_TILE_SMEM_KB", 112) * 1024;
+  const int forced = env_int("RLS_TILE_NS", 0);
+  int ns = 0;
+  if (forced >= 2 && forced <= kMaxStages) {
+    ns = forced;
+  } else {
+    for (int c = kMaxStages; c >= 2 && !ns; --c)
+      if (c * (int64_t)tg.stage_bytes + outb <= budget) ns = c;
+    if (!ns) ns = 2;
+  }
+  if (ns * (int64_t)tg.stage_bytes + outb > 220 * 1024) return RLS_EUNSUPPORTED;
+  tg.stages = ns;
+  return launch_tile_k<P, K>(p, tg, ws, ws_bytes, s);
+}
+
+constexpr int kTileK = 16;  // elements per thread: 4 float4 (fp32) or 2 x 8 bf16 per stream
+
+// Compile-time variant dispatch (truncations present, per-step bootstrap kind).
+template <class T>
+int gae_tile(const typename GaeAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+  const bool tr = p.trunc != nullptr;
+  const int pb = p.boot_kind == RLS_BOOT_FULL_ADD ? 1 : ((p.boot_kind == RLS_BOOT_FULL_SEL && tr) ? 2 : 0);
+  if (!tr && pb == 0) return launch_tile<GaeT<T, false, 0>, kTileK>(p, g, ws, wsb, s);
+  if (tr && pb == 0) return launch_tile<GaeT<T, true, 0>, kTileK>(p, g, ws, wsb, s);
+  if (tr && pb == 2) return launch_tile<GaeT<T, true, 2>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && pb == 1) return launch_tile<GaeT<T, false, 1>, kTileK>(p, g, ws, wsb, s);
+  return launch_tile<GaeT<T, true, 1>, kTileK>(p, g, ws, wsb, s);
+}
+template <class T>
+int vtrace_tile(const typename VtraceAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+  const bool tr = p.trunc != nullptr, pb = p.boot_kind == RLS_BOOT_FULL_ADD;
+  if (!tr && !pb) return launch_tile<VtraceT<T, false, false>, kTileK>(p, g, ws, wsb, s);
+  if (tr && !pb) return launch_tile<VtraceT<T, true, false>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && pb) return launch_tile<VtraceT<T, false, true>, kTileK>(p, g, ws, wsb, s);
+  return launch_tile<VtraceT<T, true, true>, kTileK>(p, g, ws, wsb, s);
+}
+template <class T>
+int lambda_tile(const typename LambdaAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+  const bool tr = p.trunc != nullptr, pb = p.boot_kind == RLS_BOOT_FULL_ADD && p.boot;
+  if (!tr && !pb) return launch_tile<LambdaT<T, false, false>, kTileK>(p, g, ws, wsb, s);
+  if (tr && !pb) return launch_tile<LambdaT<T, true, false>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && pb) return launch_tile<LambdaT<T, false, true>, kTileK>(p, g, ws, wsb, s);
+  return launch_tile<LambdaT<T, true, true>, kTileK>(p, g, ws, wsb, s);
+}
+template <class T>
+int discounted_tile(const typename DiscountedAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb,
+                    cudaStream_t s) {
+  const bool tr = p.trunc != nullptr, pb = p.boot_kind == RLS_BOOT_FULL_ADD && p.boot;
+  if (!tr && !pb) return launch_tile<DiscountedT<T, false, false>, kTileK>(p, g, ws, wsb, s);
+  if (tr && !pb) return launch_tile<DiscountedT<T, true, false>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && pb) return launch_tile<DiscountedT<T, false, true>, kTileK>(p, g, ws, wsb, s);
+  return launch_tile<DiscountedT<T, true, true>, kTileK>(p, g, ws, wsb, s);
+}
+template <class T>
+int forward_tile(const typename ForwardAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+  if (p.prev) return launch_tile<ForwardT<T, true>, kTileK>(p, g, ws, wsb, s);
+  return launch_tile<ForwardT<T, false>, kTileK>(p, g, ws, wsb, s);
+}
+
 template <class Alg, int MAXR = 4>
 int launch(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (g.M == 0) return RLS_OK;
+  if (path_mode() == 1 && use_rows<Alg>(g)) return launch_rows<Alg, MAXR>(p, g, s);
   const int r = pick_rounds(g.M, Alg::kVec, MAXR);
   if (r >= 4 && MAXR >= 4) return launch_r<Alg, (MAXR >= 4 ? 4 : 1)>(p, g, ws, ws_bytes, s);
   if (r >= 2 && MAXR >= 2) return launch_r<Alg, (MAXR >= 2 ? 2 : 1)>(p, g, ws, ws_bytes, s);
@@ -175,9 +370,11 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
   p.out0 = advantages; p.out1 = nullptr; p.boot_kind = boot_kind; p.gamma = gamma; p.gl = gl;
   if (in_dtype == RLS_F32) {
     GAE_PARAMS(float)
+    if (path_mode() == 0) return gae_tile<float>(p, g, ws, ws_bytes, s);
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     GAE_PARAMS(__nv_bfloat16)
+    if (path_mode() == 0) return gae_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef GAE_PARAMS
@@ -211,9 +408,11 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
   p.gamma = gamma; p.rho_bar = rho_bar; p.c_bar = c_bar;
   if (in_dtype == RLS_F32) {
     VT_PARAMS(float)
+    if (path_mode() == 0) return vtrace_tile<float>(p, g, ws, ws_bytes, s);
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
     VT_PARAMS(__nv_bfloat16)
+    if (path_mode() == 0) return vtrace_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef VT_PARAMS
@@ -242,6 +441,16 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   p.out0 = targets; p.out1 = advantages; p.A = num_actions;
   p.gamma = gamma; p.lam = lambda_; p.c_bar = c_bar; p.rho_bar = rho_bar;
   if (g.M == 0) return RLS_OK;
+  const int mode = path_mode();
+  if (mode == 0) {
+    // Stage pi / Qn in the tile ring while a two-stage ring of them fits.
+    const int64_t per_step = 8 * num_actions + 28;
+    const bool staged = num_actions <= 16 && 2 * per_step * kTileThreads * 9 + 12 * kTileThreads * 9 <= 220 * 1024;
+    p.warp_elems = staged ? 1 : 0;
+    if (staged) return launch_tile<RetraceT<true>, 9>(p, g, ws, ws_bytes, s);
+    return launch_tile<RetraceT<false>, 9>(p, g, ws, ws_bytes, s);
+  }
+  if (mode == 1 && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 2>(p, g, s);
   // Staging: one warp span of pi and Qn rows plus actions, E and pi_a.
   int rounds = pick_rounds(g.M, 4, 2);
   auto per_warp = [&](int r) {
@@ -282,9 +491,11 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
   p.boot_kind = boot_kind; p.gamma = gamma; p.g1l = gamma * (1.0f - lambda_); p.gl = gamma * lambda_;
   if (in_dtype == RLS_F32) {
     LAM_PARAMS(float)
+    if (path_mode() == 0) return lambda_tile<float>(p, g, ws, ws_bytes, s);
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     LAM_PARAMS(__nv_bfloat16)
+    if (path_mode() == 0) return lambda_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef LAM_PARAMS
@@ -312,9 +523,11 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
   p.boot = (const T*)bootstrap; p.out0 = out; p.out1 = nullptr; p.boot_kind = boot_kind; p.gamma = gamma;
   if (in_dtype == RLS_F32) {
     DISC_PARAMS(float)
+    if (path_mode() == 0) return discounted_tile<float>(p, g, ws, ws_bytes, s);
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     DISC_PARAMS(__nv_bfloat16)
+    if (path_mode() == 0) return discounted_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef DISC_PARAMS
@@ -337,9 +550,11 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
   p.out0 = out; p.out1 = nullptr; p.k = k; p.prev = prev;
   if (in_dtype == RLS_F32) {
     FWD_PARAMS(float)
+    if (path_mode() == 0) return forward_tile<float>(p, g, ws, ws_bytes, s);
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     FWD_PARAMS(__nv_bfloat16)
+    if (path_mode() == 0) return forward_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef FWD_PARAMS
@@ -371,9 +586,11 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
   cudaStream_t s = as_stream(stream);
   if (direction == 0) {
     AffineAlg<true>::Params p{u, v, carry, out, nullptr};
+    if (path_mode() == 0) return launch_tile<AffineT<true>, kTileK>(p, g, ws, ws_bytes, s);
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
   AffineAlg<false>::Params p{u, v, carry, out, nullptr};
+  if (path_mode() == 0) return launch_tile<AffineT<false>, kTileK>(p, g, ws, ws_bytes, s);
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }
 

@@ -55,7 +55,7 @@ scan_kernel(const typename Alg::Params p, const Geom g, void* ws_base) {
   __shared__ uint64_t s_mbar[WARPS];
   extern __shared__ __align__(128) unsigned char s_dyn[];
 
-  const Workspace ws = ws_carve(ws_base, g.num_tiles);
+  const Workspace ws = ws_carve(ws_base, g.ws_cap);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
 

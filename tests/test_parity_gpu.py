@@ -33,8 +33,17 @@ def T(a, dev="cuda", dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)
 
 
+@pytest.fixture(autouse=True, params=["tile", "rows", "flat"])
+def kernel_path(request, monkeypatch):
+    """Run every case on each kernel family: the TMA-staged tile kernel (the
+    default), the row-parallel register kernel (one warp per row) and the flat
+    register kernel with decoupled look-back."""
+    monkeypatch.setenv("RLS_PATH", request.param)
+    return request.param
+
+
 @pytest.fixture(autouse=True)
-def _no_device_errors():
+def _no_device_errors(kernel_path):
     _cuda()
     yield
     from rl_triton import _native as nat
