@@ -42,6 +42,7 @@ extern "C" {
 #define RLS_EWORKSPACE    3   /* workspace missing or too small            */
 #define RLS_ECUDA         4   /* CUDA launch / runtime error               */
 #define RLS_EUNSUPPORTED  5   /* combination not implemented               */
+#define RLS_ETOOLARGE     6   /* larger than rls_gae_noalloc's fixed scratch */
 
 /* ---- input element types --------------------------------------------- */
 #define RLS_F32   0
@@ -194,6 +195,32 @@ int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtyp
                       float* out, const float* carry,
                       int64_t num_envs, int64_t seq_len, float coef, int flags,
                       const rls_segment_t* seg, void* stream);
+
+/* ---- GAE for callers that cannot allocate --------------------------------
+ * No counterpart in the reference (its Triton path always allocates through
+ * PyTorch).  Same arguments and results as rls_gae, minus the workspace: the
+ * look-back scratch lives in a fixed array inside the library
+ * (RLS_NOALLOC_MAX_ELEMENTS elements' worth, about 5 MB, held on every GPU
+ * that loads the library until the process exits).  Meant for callers that
+ * must not call cudaMalloc -- code running while a CUDA graph is being
+ * captured into a pool they do not own, real-time loops with a frozen memory
+ * budget, or hosts that only hand out buffers they allocated themselves.
+ *  - num_envs * seq_len above RLS_NOALLOC_MAX_ELEMENTS returns RLS_ETOOLARGE.
+ *  - The call allocates nothing; it clears the scratch's counters with two
+ *    small cudaMemsetAsync on `stream`, then launches the same kernels as
+ *    rls_gae.
+ *  - The first call on a device looks the array's device address up
+ *    (cudaGetSymbolAddress); make that first call before any stream capture.
+ *  - Every call shares the one array: calls that may overlap on the GPU (on
+ *    different streams without ordering between them) race and give wrong
+ *    results.  Order them on one stream, or use rls_gae with a workspace per
+ *    stream.                                                                */
+#define RLS_NOALLOC_MAX_ELEMENTS (1LL << 27)
+int rls_gae_noalloc(const void* rewards, const void* values, const void* terminateds,
+                    const void* truncateds, const void* bootstrap, int boot_kind,
+                    float* advantages, int64_t num_envs, int64_t seq_len,
+                    float gamma, float lambda_, int in_dtype,
+                    const rls_segment_t* seg, void* stream);
 
 #ifdef __cplusplus
 }

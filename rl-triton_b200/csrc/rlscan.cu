@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <mutex>
 
 #include "rlscan.h"
 #include "scan_kernel.cuh"
@@ -333,6 +334,7 @@ const char* rls_status_string(int status) {
       return buf;
     }
     case RLS_EUNSUPPORTED: return "unsupported argument combination";
+    case RLS_ETOOLARGE: return "num_envs * seq_len exceeds RLS_NOALLOC_MAX_ELEMENTS (the fixed scratch of rls_gae_noalloc)";
     default: return "unknown status";
   }
 }
@@ -595,3 +597,52 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// rls_gae_noalloc: GAE whose look-back scratch is a fixed array in this file,
+// for callers that cannot allocate device memory.  The array is sized for the
+// smallest tiles any GAE launch uses (kMinTileElems elements), so every path
+// (tile, row, flat) fits up to RLS_NOALLOC_MAX_ELEMENTS elements.  It starts
+// zero-filled, as the look-back protocol requires; the kernels keep it
+// consistent from call to call (epoch-tagged flags), and each call clears the
+// ticket / exit counters and the error latch before launching.
+namespace {
+constexpr int64_t kNoAllocTiles = RLS_NOALLOC_MAX_ELEMENTS / kMinTileElems;
+constexpr size_t kNoAllocBytes = 64 + (size_t)kNoAllocTiles * 4 + (size_t)kNoAllocTiles * 16;
+static_assert(kNoAllocTiles * 4 % 16 == 0, "flag array keeps the aggregate array 16-byte aligned");
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+}  // namespace
+
+static __device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocBytes];
+
+extern "C" int rls_gae_noalloc(const void* rewards, const void* values, const void* terminateds,
+                               const void* truncateds, const void* bootstrap, int boot_kind, float* advantages,
+                               int64_t num_envs, int64_t seq_len, float gamma, float lambda_, int in_dtype,
+                               const rls_segment_t* seg, void* stream) {
+  if (num_envs < 0 || seq_len < 0) return RLS_EINVAL;
+  if (num_envs == 0 || seq_len == 0) return RLS_OK;
+  if (num_envs > RLS_NOALLOC_MAX_ELEMENTS / seq_len) return RLS_ETOOLARGE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RLS_ECUDA;
+  void* ws = nullptr;
+  {
+    // Set-up, once per device with that device current: the host-side name of
+    // the array is not a device address, so look the address up.
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_ws) != cudaSuccess || !p) return RLS_ECUDA;
+      g_noalloc_ptr[dev] = p;
+    }
+    ws = g_noalloc_ptr[dev];
+  }
+  cudaStream_t s = as_stream(stream);
+  // Ticket and exit counters (bytes 0-7) and the error latch (12-15); the
+  // epoch (8-11) must keep counting up.
+  if (cudaMemsetAsync(ws, 0, 8, s) != cudaSuccess) return RLS_ECUDA;
+  if (cudaMemsetAsync((char*)ws + 12, 0, 4, s) != cudaSuccess) return RLS_ECUDA;
+  return rls_gae(rewards, values, terminateds, truncateds, bootstrap, boot_kind, advantages, num_envs, seq_len,
+                 gamma, lambda_, in_dtype, seg, ws, kNoAllocBytes, stream);
+}

@@ -18,6 +18,8 @@ LIB_PATH = os.environ.get("RLSCAN_LIB", os.path.join(_HERE, "_lib", "librlscan.s
 RLS_OK = 0
 RLS_F32 = 0
 RLS_BF16 = 1
+RLS_ETOOLARGE = 6
+NOALLOC_MAX_ELEMENTS = 1 << 27
 
 BOOT_NONE = 0
 BOOT_ROW = 1
@@ -73,6 +75,7 @@ _SIGS = {
     "rls_affine_scan": (_I, [_P, _P, _P, _I, _P, _I64, _I64, _SEG, _P, _SZ, _P]),
     "rls_segment_reduce": (_I, [_I, _P, _P, _I, _P, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
     "rls_segment_fixup": (_I, [_I, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
+    "rls_gae_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _F, _F, _I, _SEG, _P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
