@@ -74,8 +74,8 @@ __host__ __device__ inline size_t ws_bytes_for_tiles(int64_t ntiles) {
 // one buffer sees the flags, aggregates and inclusive values at the same
 // places, and a stale aggregate can never be read as another launch's flag.
 __host__ __device__ inline int64_t ws_capacity(size_t bytes) {
-  if (bytes < 64 + 16 + 20) return 0;
-  int64_t cap = (int64_t)((bytes - 64 - 16) / 20);
+  if (bytes < 64 + 20) return 0;
+  int64_t cap = (int64_t)((bytes - 64) / 20);
   while (cap > 0 && ws_bytes_for_tiles(cap) > bytes) --cap;
   return cap;
 }

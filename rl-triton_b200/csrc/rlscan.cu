@@ -108,15 +108,29 @@ int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
   return launch_rows_r<Alg, 1>(p, g, s);
 }
 
-// ---- TMA-staged tile path (default) ----------------------------------------
-// Which kernel family serves a call: RLS_PATH=tile (default) | rows | flat.
-// rows/flat are the register-only kernels, kept as cross-checks.
+// ---- kernel family ----------------------------------------------------------
+// RLS_PATH=auto (default) | rows | flat | tile.  auto: the row kernel when every
+// row starts 16-byte aligned and there are enough rows to fill the GPU (one
+// warp per row, no workspace, no barrier), else the TMA-staged tile kernel,
+// which also parallelises along time.  rows / flat / tile force one family
+// (rows falls back to flat when rows are not aligned).
 int path_mode() {
   const char* s = std::getenv("RLS_PATH");
   if (!s || !*s) return 0;
   if (!std::strcmp(s, "rows")) return 1;
   if (!std::strcmp(s, "flat")) return 2;
+  if (!std::strcmp(s, "tile")) return 3;
   return 0;
+}
+
+constexpr int64_t kRowsMinEnvs = 8 * 148;  // rows that give every SM 8 warps
+
+template <class Alg>
+bool tile_first(const Geom& g) {
+  const int m = path_mode();
+  if (m == 3) return true;
+  if (m != 0) return false;
+  return !(g.S % Alg::kVec == 0 && g.N >= kRowsMinEnvs);
 }
 
 int num_sms(int dev) {
@@ -266,7 +280,8 @@ int forward_tile(const typename ForwardAlg<T>::Params& p, const Geom& g, void* w
 template <class Alg, int MAXR = 4>
 int launch(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (g.M == 0) return RLS_OK;
-  if (path_mode() == 1 && use_rows<Alg>(g)) return launch_rows<Alg, MAXR>(p, g, s);
+  const int pm = path_mode();
+  if ((pm == 0 || pm == 1) && use_rows<Alg>(g)) return launch_rows<Alg, MAXR>(p, g, s);
   const int r = pick_rounds(g.M, Alg::kVec, MAXR);
   if (r >= 4 && MAXR >= 4) return launch_r<Alg, (MAXR >= 4 ? 4 : 1)>(p, g, ws, ws_bytes, s);
   if (r >= 2 && MAXR >= 2) return launch_r<Alg, (MAXR >= 2 ? 2 : 1)>(p, g, ws, ws_bytes, s);
@@ -372,11 +387,11 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
   p.out0 = advantages; p.out1 = nullptr; p.boot_kind = boot_kind; p.gamma = gamma; p.gl = gl;
   if (in_dtype == RLS_F32) {
     GAE_PARAMS(float)
-    if (path_mode() == 0) return gae_tile<float>(p, g, ws, ws_bytes, s);
+    if (tile_first<GaeAlg<float>>(g)) return gae_tile<float>(p, g, ws, ws_bytes, s);
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     GAE_PARAMS(__nv_bfloat16)
-    if (path_mode() == 0) return gae_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    if (tile_first<GaeAlg<__nv_bfloat16>>(g)) return gae_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef GAE_PARAMS
@@ -410,11 +425,11 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
   p.gamma = gamma; p.rho_bar = rho_bar; p.c_bar = c_bar;
   if (in_dtype == RLS_F32) {
     VT_PARAMS(float)
-    if (path_mode() == 0) return vtrace_tile<float>(p, g, ws, ws_bytes, s);
+    if (tile_first<VtraceAlg<float>>(g)) return vtrace_tile<float>(p, g, ws, ws_bytes, s);
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
     VT_PARAMS(__nv_bfloat16)
-    if (path_mode() == 0) return vtrace_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    if (tile_first<VtraceAlg<__nv_bfloat16>>(g)) return vtrace_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef VT_PARAMS
@@ -444,7 +459,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   p.gamma = gamma; p.lam = lambda_; p.c_bar = c_bar; p.rho_bar = rho_bar;
   if (g.M == 0) return RLS_OK;
   const int mode = path_mode();
-  if (mode == 0) {
+  if (tile_first<RetraceAlg>(g)) {
     // Stage pi / Qn in the tile ring while a two-stage ring of them fits.
     const int64_t per_step = 8 * num_actions + 28;
     const bool staged = num_actions <= 16 && 2 * per_step * kTileThreads * 9 + 12 * kTileThreads * 9 <= 220 * 1024;
@@ -452,7 +467,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
     if (staged) return launch_tile<RetraceT<true>, 9>(p, g, ws, ws_bytes, s);
     return launch_tile<RetraceT<false>, 9>(p, g, ws, ws_bytes, s);
   }
-  if (mode == 1 && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 2>(p, g, s);
+  if ((mode == 0 || mode == 1) && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 2>(p, g, s);
   // Staging: one warp span of pi and Qn rows plus actions, E and pi_a.
   int rounds = pick_rounds(g.M, 4, 2);
   auto per_warp = [&](int r) {
@@ -493,11 +508,11 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
   p.boot_kind = boot_kind; p.gamma = gamma; p.g1l = gamma * (1.0f - lambda_); p.gl = gamma * lambda_;
   if (in_dtype == RLS_F32) {
     LAM_PARAMS(float)
-    if (path_mode() == 0) return lambda_tile<float>(p, g, ws, ws_bytes, s);
+    if (tile_first<LambdaAlg<float>>(g)) return lambda_tile<float>(p, g, ws, ws_bytes, s);
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     LAM_PARAMS(__nv_bfloat16)
-    if (path_mode() == 0) return lambda_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    if (tile_first<LambdaAlg<__nv_bfloat16>>(g)) return lambda_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef LAM_PARAMS
@@ -525,11 +540,11 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
   p.boot = (const T*)bootstrap; p.out0 = out; p.out1 = nullptr; p.boot_kind = boot_kind; p.gamma = gamma;
   if (in_dtype == RLS_F32) {
     DISC_PARAMS(float)
-    if (path_mode() == 0) return discounted_tile<float>(p, g, ws, ws_bytes, s);
+    if (tile_first<DiscountedAlg<float>>(g)) return discounted_tile<float>(p, g, ws, ws_bytes, s);
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     DISC_PARAMS(__nv_bfloat16)
-    if (path_mode() == 0) return discounted_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    if (tile_first<DiscountedAlg<__nv_bfloat16>>(g)) return discounted_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef DISC_PARAMS
@@ -552,11 +567,11 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
   p.out0 = out; p.out1 = nullptr; p.k = k; p.prev = prev;
   if (in_dtype == RLS_F32) {
     FWD_PARAMS(float)
-    if (path_mode() == 0) return forward_tile<float>(p, g, ws, ws_bytes, s);
+    if (tile_first<ForwardAlg<float>>(g)) return forward_tile<float>(p, g, ws, ws_bytes, s);
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     FWD_PARAMS(__nv_bfloat16)
-    if (path_mode() == 0) return forward_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    if (tile_first<ForwardAlg<__nv_bfloat16>>(g)) return forward_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef FWD_PARAMS
@@ -588,11 +603,11 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
   cudaStream_t s = as_stream(stream);
   if (direction == 0) {
     AffineAlg<true>::Params p{u, v, carry, out, nullptr};
-    if (path_mode() == 0) return launch_tile<AffineT<true>, kTileK>(p, g, ws, ws_bytes, s);
+    if (tile_first<AffineAlg<true>>(g)) return launch_tile<AffineT<true>, kTileK>(p, g, ws, ws_bytes, s);
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
   AffineAlg<false>::Params p{u, v, carry, out, nullptr};
-  if (path_mode() == 0) return launch_tile<AffineT<false>, kTileK>(p, g, ws, ws_bytes, s);
+  if (tile_first<AffineAlg<false>>(g)) return launch_tile<AffineT<false>, kTileK>(p, g, ws, ws_bytes, s);
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }
 

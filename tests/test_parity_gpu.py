@@ -33,12 +33,15 @@ def T(a, dev="cuda", dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)
 
 
-@pytest.fixture(autouse=True, params=["tile", "rows", "flat"])
+@pytest.fixture(autouse=True, params=["auto", "tile", "rows", "flat"])
 def kernel_path(request, monkeypatch):
-    """Run every case on each kernel family: the TMA-staged tile kernel (the
-    default), the row-parallel register kernel (one warp per row) and the flat
-    register kernel with decoupled look-back."""
-    monkeypatch.setenv("RLS_PATH", request.param)
+    """Run every case on each kernel family: the library's own choice ("auto"),
+    the TMA-staged tile kernel, the row-parallel register kernel (one warp per
+    row) and the flat register kernel with decoupled look-back."""
+    if request.param == "auto":
+        monkeypatch.delenv("RLS_PATH", raising=False)
+    else:
+        monkeypatch.setenv("RLS_PATH", request.param)
     return request.param
 
 
