@@ -67,8 +67,9 @@ CONFIGS = {
                  desc="config 4: GAE + V-trace, num_envs=131072 seq_len=1024, bf16 inputs, fp32 out (per GPU)"),
     "cfg5a": dict(N=64, T=131072, trunc=False, bf16=False, funcs=["vtrace"], p_term=0.01,
                   desc="config 5a: V-trace num_envs=64 seq_len=131072 fp32"),
-    "cfg5b": dict(N=1, T=1 << 28, trunc=False, bf16=False, funcs=["prefix", "gae"], p_term=1e-4,
-                  desc="config 5b (single GPU part): prefix sum + GAE, num_envs=1 seq_len=2^28 fp32"),
+    "cfg5b": dict(N=1, T=1 << 28, trunc=False, bf16=False, funcs=["prefix", "gae"], p_term=1e-4, split=True,
+                  desc="config 5b: prefix sum + GAE, num_envs=1 seq_len=2^28 fp32; under torchrun the sequence "
+                       "is split along time across the ranks (carry exchange over NCCL)"),
 }
 
 
@@ -119,9 +120,18 @@ def make_inputs(cfg, device, seed, gen_device=None):
     return x
 
 
-def make_calls(cfg, x):
-    """The public-API calls of one step (drop-in rl_triton)."""
+def make_calls(cfg, x, split=False):
+    """The public-API calls of one step (drop-in rl_triton; rl_triton.dist when
+    the sequence is split along time across the ranks)."""
     import rl_triton
+
+    if split:
+        from rl_triton import dist as D
+
+        return {k: v for k, v in {
+            "prefix": lambda: D.compute_episodic_prefix_sum(x["r"], x["term"]),
+            "gae": lambda: D.compute_gae(x["r"], x["v"], x["term"], gamma=0.99, lambda_=0.95),
+        }.items() if k in cfg["funcs"]}
 
     tr = cfg["trunc"]
     calls = {}
@@ -363,6 +373,9 @@ def run_reference(args, world, rank):
 
 def run_b200(args, world, rank, local):
     cfg = CONFIGS[args.config]
+    split = world > 1 and cfg.get("split", False)
+    if split:  # strong scaling: each rank holds T / world columns of the one sequence
+        cfg = dict(cfg, T=cfg["T"] // world)
     dev = torch.device("cuda", local)
     from rl_triton import _native as nat
 
@@ -372,7 +385,7 @@ def run_b200(args, world, rank, local):
     if args.sets:
         n_sets = args.sets
     sets = [make_inputs(cfg, dev, seed=1000 * rank + k) for k in range(n_sets)]
-    calls = [make_calls(cfg, x) for x in sets]
+    calls = [make_calls(cfg, x, split) for x in sets]
     stream = torch.cuda.Stream(dev)
 
     # Warm up on the capture stream (allocates this stream's workspace).
@@ -382,7 +395,7 @@ def run_b200(args, world, rank, local):
                 f()
     stream.synchronize()
 
-    use_graph = not args.no_graph
+    use_graph = not args.no_graph and not split  # the time split reads lengths on the host
     graphs = []
     if use_graph:
         for c in calls:
@@ -428,15 +441,24 @@ def run_b200(args, world, rank, local):
     hbm, peak_kind = peaks()
     reps = max(8, min(200, args.steps))
     for fname in cfg["funcs"]:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
-            for k in range(reps):
-                calls[k % n_sets][fname]()
+        g = None
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for k in range(reps):
+                    calls[k % n_sets][fname]()
         with torch.cuda.stream(stream):
-            g.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            g.replay()
+            if g is not None:
+                g.replay()
+                e0.record(stream)
+                g.replay()
+            else:
+                for k in range(reps):
+                    calls[k % n_sets][fname]()
+                e0.record(stream)
+                for k in range(reps):
+                    calls[k % n_sets][fname]()
             e1.record(stream)
         stream.synchronize()
         us = e0.elapsed_time(e1) * 1e3 / reps
@@ -461,7 +483,7 @@ def run_b200(args, world, rank, local):
         def e2e_step():
             xd = {k: v.to(dev, non_blocking=True) for k, v in host.items() if _used(k, cfg)}
             res = []
-            for f in make_calls(cfg, xd).values():
+            for f in make_calls(cfg, xd, split).values():
                 r = f()
                 res.extend(r if isinstance(r, tuple) else (r,))
             outs = [r.to("cpu", non_blocking=True) for r in res]
@@ -499,10 +521,12 @@ def run_b200(args, world, rank, local):
         line = {
             "metric": "timesteps/sec", "value": value, "unit": "timesteps/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16->f32" if cfg["bf16"] else "f32",
+            "scaling": "strong" if split else "weak", "vs_baseline": None,
+            "dtype": "bf16->f32" if cfg["bf16"] else "f32",
             "data": "synthetic (seeded torch.Generator; BASELINE config distributions)",
             "config": {"workload": cfg["desc"], "functions": cfg["funcs"], "num_envs_per_gpu": N,
-                       "seq_len": T, "parallelism": f"env-sharded x{world}" if world > 1 else "single GPU",
+                       "seq_len": T, "parallelism": (f"time-split x{world}" if split else f"env-sharded x{world}") if world > 1
+                       else "single GPU",
                        "l2": f"{n_sets} rotating input sets ({per_set * n_sets / 1e6:.0f} MB > 126 MB L2)",
                        "launch": "CUDA graph per input set" if use_graph else "eager"},
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": d["achieved_gbs"], "peak": hbm,
