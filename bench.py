@@ -128,9 +128,11 @@ def make_calls(cfg, x, split=False):
     if split:
         from rl_triton import dist as D
 
+        rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+        lay = dict(t0=rank * cfg["T"], total=world * cfg["T"])  # equal segments: no length exchange
         return {k: v for k, v in {
-            "prefix": lambda: D.compute_episodic_prefix_sum(x["r"], x["term"]),
-            "gae": lambda: D.compute_gae(x["r"], x["v"], x["term"], gamma=0.99, lambda_=0.95),
+            "prefix": lambda: D.compute_episodic_prefix_sum(x["r"], x["term"], **lay),
+            "gae": lambda: D.compute_gae(x["r"], x["v"], x["term"], gamma=0.99, lambda_=0.95, **lay),
         }.items() if k in cfg["funcs"]}
 
     tr = cfg["trunc"]

@@ -11,8 +11,12 @@
 // after a few thousand steps when b < 1, so both walks stop early; a segment
 // without any reset is still handled, just by walking all of it.
 //
-// One warp per row walks 32 elements per step from the edge inward with a
-// shuffle product scan.
+// Many rows: one warp per row walks 32 elements per step from the edge inward
+// with a shuffle product scan.  Few rows (a single long sequence split across
+// GPUs): one 512-thread block per row walks 2048 elements per step with a
+// block-wide product scan, so the walk to the first reset (~10^4 steps for a
+// 1e-4 done rate) takes a handful of steps instead of hundreds of dependent
+// loads.
 #include "rlscan.h"
 #include "common.cuh"
 
@@ -111,6 +115,86 @@ __global__ void __launch_bounds__(128) segment_walk(const SegArgs a) {
   }
 }
 
+constexpr int kBlockWalk = 512;   // threads of the block-per-row walk
+constexpr int kBlockElems = 4;    // consecutive (walk-order) elements per thread
+
+// Block-per-row version of segment_walk (same results up to the rounding of
+// the decay products).
+template <int MODE>
+__global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a) {
+  constexpr int NW = kBlockWalk / 32;
+  constexpr int STEP = kBlockWalk * kBlockElems;
+  __shared__ float s_w[NW];
+  __shared__ float s_base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = blockIdx.x;
+  const int64_t S = a.S;
+  float c = 0.f;
+  if (MODE == 1) {
+    c = a.carry[row];
+    if (c == 0.f || a.global_edge) return;  // uniform across the block
+  }
+  float base = 1.f;  // product of b over all earlier steps
+  bool zero = (MODE == 0) && a.global_edge;
+  for (int64_t k0 = 0; k0 < S && !zero; k0 += STEP) {
+    float b[kBlockElems];
+    int64_t col[kBlockElems];
+#pragma unroll
+    for (int q = 0; q < kBlockElems; ++q) {
+      const int64_t k = k0 + (int64_t)threadIdx.x * kBlockElems + q;
+      col[q] = k < S ? (a.backward ? (S - 1 - k) : k) : -1;
+      b[q] = col[q] >= 0 ? decay_at(a, row, col[q]) : 1.f;
+    }
+    float mine = 1.f;
+#pragma unroll
+    for (int q = 0; q < kBlockElems; ++q) mine *= b[q];
+    float incl = mine;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl *= o;
+    }
+    if (lane == 31) s_w[warp] = incl;
+    __syncthreads();
+    float before = 1.f, total = 1.f;
+    for (int w = 0; w < NW; ++w) {
+      if (w == warp) before = total;
+      total *= s_w[w];
+    }
+    const float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    float P = base * before * (lane == 0 ? 1.f : excl);
+    if (MODE == 1) {
+#pragma unroll
+      for (int q = 0; q < kBlockElems; ++q) {
+        P *= b[q];
+        if (col[q] >= 0 && P != 0.f) {
+          float* o = a.out + row * S + col[q];
+          *o = fmaf(P, c, *o);
+        }
+      }
+    }
+    if (threadIdx.x == 0) s_base = base * total;
+    __syncthreads();
+    base = s_base;
+    if (base == 0.f) zero = true;
+    __syncthreads();  // s_w / s_base are rewritten next step
+  }
+  if (MODE == 0 && threadIdx.x == 0) {
+    const int64_t far = a.backward ? 0 : (S - 1);
+    a.seg_a[row] = S > 0 ? a.out[row * S + far] : 0.f;
+    a.seg_b[row] = zero ? 0.f : base;
+  }
+}
+
+// Few rows: a block per row; many rows: a warp per row.
+template <int MODE>
+int launch_walk(const SegArgs& a, void* stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (a.N <= 64) segment_walk_block<MODE><<<(unsigned)a.N, kBlockWalk, 0, s>>>(a);
+  else segment_walk<MODE><<<(unsigned)((a.N + 3) / 4), 128, 0, s>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+}
+
 int fill_args(int alg, const void* flag0, const void* flag1, int in_dtype, int64_t N, int64_t S, float coef,
               int flags, const rls_segment_t* seg, SegArgs& a) {
   if (alg < RLS_ALG_GAE || alg > RLS_ALG_SCAN_FWD || !flag0 || !seg || N < 0 || S < 0) return RLS_EINVAL;
@@ -148,9 +232,7 @@ int rls_segment_reduce(int alg, const void* flag0, const void* flag1, int in_dty
   a.seg_a = seg_a;
   a.seg_b = seg_b;
   if (num_envs == 0) return RLS_OK;
-  const unsigned blocks = (unsigned)((num_envs + 3) / 4);
-  segment_walk<0><<<blocks, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  return launch_walk<0>(a, stream);
 }
 
 int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtype, float* out, const float* carry,
@@ -165,9 +247,7 @@ int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtyp
   a.seg_a = nullptr;
   a.seg_b = nullptr;
   if (num_envs == 0) return RLS_OK;
-  const unsigned blocks = (unsigned)((num_envs + 3) / 4);
-  segment_walk<1><<<blocks, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  return launch_walk<1>(a, stream);
 }
 
 }  // extern "C"

@@ -5,7 +5,8 @@ No counterpart in the reference, which runs every scan on one device
 [t0_k, t0_k + S_k) of every row (its *segment*), with t0 given by the ranks'
 order.  Each call:
 
-1. exchanges the segment lengths and the one-column halos the recurrences
+1. exchanges the segment lengths (unless the caller passes `t0` and `total`,
+   which spares a host synchronisation) and the one-column halos the recurrences
    read across a cut: backward GAE needs the next segment's first value
    V[t0+S]; the forward scans gated by done[t-1] need the previous segment's
    last flag;
@@ -115,7 +116,7 @@ def _rank_world(group):
 
 
 def _run(alg, x: dict, p: dict, ref: torch.Tensor, group=None, all_gather=None, kernels=None, rank=None,
-         world=None) -> torch.Tensor:
+         world=None, t0=None, total=None) -> torch.Tensor:
     if all_gather is None:
         all_gather = torch_all_gather(group)
         rank, world = _rank_world(group)
@@ -132,11 +133,12 @@ def _run(alg, x: dict, p: dict, ref: torch.Tensor, group=None, all_gather=None, 
         edge = x["dones"][:, -1].float()           # our last flag: the next rank's halo
     else:
         edge = torch.zeros(n, dtype=torch.float32, device=dev)
-    meta = torch.cat([torch.tensor([float(s)], device=dev), edge])
+    meta = torch.cat([torch.full((1,), float(s), dtype=torch.float32, device=dev), edge])
     metas = all_gather(meta)
-    lengths = [int(m[0].item()) for m in metas]
-    t0 = sum(lengths[:rank])
-    seg = Segment(rank, world, t0, s, sum(lengths))
+    if t0 is None or total is None:  # learn the layout (reads the lengths on the host)
+        lengths = [int(m[0].item()) for m in metas]
+        t0, total = sum(lengths[:rank]), sum(lengths)
+    seg = Segment(rank, world, t0, s, total)
     halo = None
     if alg == GAE and rank + 1 < world:
         halo = metas[rank + 1][1:].contiguous()
@@ -159,42 +161,42 @@ def _run(alg, x: dict, p: dict, ref: torch.Tensor, group=None, all_gather=None, 
 
 
 def compute_gae(rewards, values, terminateds, truncateds=None, gamma=0.99, lambda_=0.95, last_value=None, *,
-                group=None, all_gather=None, kernels=None, rank=None, world=None):
+                group=None, all_gather=None, kernels=None, rank=None, world=None, t0=None, total=None):
     """GAE over a sequence split along time; arguments are this rank's columns.
     `last_value` is read by the rank that holds the window end."""
     x = dict(rewards=rewards, values=values, terminateds=terminateds, truncateds=truncateds, last_value=last_value)
     p = dict(gamma=gamma, lambda_=lambda_, coef=gamma * lambda_, flags=0)
-    return _run(GAE, x, p, rewards, group, all_gather, kernels, rank, world)
+    return _run(GAE, x, p, rewards, group, all_gather, kernels, rank, world, t0, total)
 
 
 def compute_lambda_returns(rewards, next_values, terminateds, truncateds=None, gamma=0.99, lambda_=0.95, *,
-                           group=None, all_gather=None, kernels=None, rank=None, world=None):
+                           group=None, all_gather=None, kernels=None, rank=None, world=None, t0=None, total=None):
     x = dict(rewards=rewards, next_values=next_values, terminateds=terminateds, truncateds=truncateds)
     p = dict(gamma=gamma, lambda_=lambda_, coef=gamma * lambda_, flags=0)
-    return _run(LAMBDA, x, p, rewards, group, all_gather, kernels, rank, world)
+    return _run(LAMBDA, x, p, rewards, group, all_gather, kernels, rank, world, t0, total)
 
 
 def compute_discounted_returns(rewards, terminateds, truncateds=None, gamma=0.99, *, group=None, all_gather=None,
-                               kernels=None, rank=None, world=None):
+                               kernels=None, rank=None, world=None, t0=None, total=None):
     x = dict(rewards=rewards, terminateds=terminateds, truncateds=truncateds)
     p = dict(gamma=gamma, coef=gamma, flags=0)
-    return _run(DISCOUNTED, x, p, rewards, group, all_gather, kernels, rank, world)
+    return _run(DISCOUNTED, x, p, rewards, group, all_gather, kernels, rank, world, t0, total)
 
 
 def compute_eligibility_traces(gradients, dones, gamma, lambda_, seed_values=None, *, group=None, all_gather=None,
-                               kernels=None, rank=None, world=None):
+                               kernels=None, rank=None, world=None, t0=None, total=None):
     """Traces over a sequence split along time; `seed_values` is read by rank 0."""
     x = dict(inputs=gradients, dones=dones, seed_values=seed_values)
     p = dict(gamma=gamma, lambda_=lambda_, coef=gamma * lambda_, flags=0)
-    return _run(ELIGIBILITY, x, p, gradients, group, all_gather, kernels, rank, world)
+    return _run(ELIGIBILITY, x, p, gradients, group, all_gather, kernels, rank, world, t0, total)
 
 
 def compute_episodic_prefix_sum(inputs, dones, seed_values=None, boundary="ends_at", *, group=None, all_gather=None,
-                                kernels=None, rank=None, world=None):
+                                kernels=None, rank=None, world=None, t0=None, total=None):
     """Episodic prefix sum over a sequence split along time; `seed_values` is read by rank 0."""
     x = dict(inputs=inputs, dones=dones, seed_values=seed_values)
     p = dict(boundary=boundary, coef=1.0, flags=1 if boundary == "ends_at" else 0)
-    return _run(PREFIX, x, p, inputs, group, all_gather, kernels, rank, world)
+    return _run(PREFIX, x, p, inputs, group, all_gather, kernels, rank, world, t0, total)
 
 
 def split_columns(t: torch.Tensor, rank: int, world: int) -> torch.Tensor:
