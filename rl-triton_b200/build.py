@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "rl_triton", "_lib")
 LIB = os.path.join(LIBDIR, "librlscan.so")
 SOURCES = ["rlscan.cu", "segment.cu"]
-HEADERS = ["common.cuh", "algs.cuh", "scan_kernel.cuh", "rows_kernel.cuh", "tile_kernel.cuh", "tile_policies.cuh"]
+HEADERS = ["common.cuh", "algs.cuh", "scan_kernel.cuh", "rows_kernel.cuh", "rows2_kernel.cuh", "tile_kernel.cuh", "tile_policies.cuh"]
 
 
 def nvcc_path() -> str:

@@ -13,6 +13,7 @@
 #include "scan_kernel.cuh"
 #include "rows_kernel.cuh"
 #include "tile_policies.cuh"
+#include "rows2_kernel.cuh"
 
 using namespace rls;
 
@@ -109,29 +110,25 @@ int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
 }
 
 // ---- kernel family ----------------------------------------------------------
-// RLS_PATH=auto (default) | rows | flat | tile.  auto: the row kernel when every
-// row starts 16-byte aligned and there are enough rows to fill the GPU (one
-// warp per row, no workspace, no barrier), else the TMA-staged tile kernel,
-// which also parallelises along time.  rows / flat / tile force one family
-// (rows falls back to flat when rows are not aligned).
+// RLS_PATH=auto (default) | rows2 | rows | flat | tile.  auto: the lean row
+// kernel (rows2) when every row starts 16-byte aligned and there are enough
+// rows to fill the GPU (one warp per row, no workspace, no barrier), else the
+// TMA-staged tile kernel, which also parallelises along time.  The others
+// force one family (the row kernels fall back to flat when rows are not
+// aligned); rows is the first row kernel with generic policies, kept as a
+// cross-check and for Retrace.
 int path_mode() {
   const char* s = std::getenv("RLS_PATH");
   if (!s || !*s) return 0;
   if (!std::strcmp(s, "rows")) return 1;
   if (!std::strcmp(s, "flat")) return 2;
   if (!std::strcmp(s, "tile")) return 3;
+  if (!std::strcmp(s, "rows2")) return 4;
   return 0;
 }
 
 constexpr int64_t kRowsMinEnvs = 8 * 148;  // rows that give every SM 8 warps
 
-template <class Alg>
-bool tile_first(const Geom& g) {
-  const int m = path_mode();
-  if (m == 3) return true;
-  if (m != 0) return false;
-  return !(g.S % Alg::kVec == 0 && g.N >= kRowsMinEnvs);
-}
 
 int num_sms(int dev) {
   static int cache[64] = {0};
@@ -235,46 +232,82 @@ int launch_tile(const typename P::Params& p, const Geom& g, void* ws, size_t ws_
 
 constexpr int kTileK = 16;  // elements per thread: 4 float4 (fp32) or 2 x 8 bf16 per stream
 
+// Launchers of the two kernels that take the compile-time policies.
+template <class P>
+struct TileL {
+  static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+    return launch_tile<P, kTileK>(p, g, ws, wsb, s);
+  }
+};
+template <class P>
+struct Rows2L {
+  static int run(const typename P::Params& p, const Geom& g, void*, size_t, cudaStream_t s) {
+    const int forced = env_int("RLS_ROWS2_R", 0);
+    const int r = forced ? forced : 1;  // one round per chunk: the leanest registers measured fastest
+    const int64_t blocks = (g.N + 3) / 4;
+    if (blocks > 0x7fffffffLL) return RLS_EINVAL;
+    if (r >= 2) rows2_kernel<P, 4, 2><<<(unsigned)blocks, 128, 0, s>>>(p, g);
+    else rows2_kernel<P, 4, 1><<<(unsigned)blocks, 128, 0, s>>>(p, g);
+    return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  }
+};
+
 // Compile-time variant dispatch (truncations present, per-step bootstrap kind).
-template <class T>
-int gae_tile(const typename GaeAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+template <template <class> class L, class T>
+int gae_v(const typename GaeAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
   const bool tr = p.trunc != nullptr;
   const int pb = p.boot_kind == RLS_BOOT_FULL_ADD ? 1 : ((p.boot_kind == RLS_BOOT_FULL_SEL && tr) ? 2 : 0);
-  if (!tr && pb == 0) return launch_tile<GaeT<T, false, 0>, kTileK>(p, g, ws, wsb, s);
-  if (tr && pb == 0) return launch_tile<GaeT<T, true, 0>, kTileK>(p, g, ws, wsb, s);
-  if (tr && pb == 2) return launch_tile<GaeT<T, true, 2>, kTileK>(p, g, ws, wsb, s);
-  if (!tr && pb == 1) return launch_tile<GaeT<T, false, 1>, kTileK>(p, g, ws, wsb, s);
-  return launch_tile<GaeT<T, true, 1>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && pb == 0) return L<GaeT<T, false, 0>>::run(p, g, ws, wsb, s);
+  if (tr && pb == 0) return L<GaeT<T, true, 0>>::run(p, g, ws, wsb, s);
+  if (tr && pb == 2) return L<GaeT<T, true, 2>>::run(p, g, ws, wsb, s);
+  if (!tr && pb == 1) return L<GaeT<T, false, 1>>::run(p, g, ws, wsb, s);
+  return L<GaeT<T, true, 1>>::run(p, g, ws, wsb, s);
 }
-template <class T>
-int vtrace_tile(const typename VtraceAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+template <template <class> class L, class T>
+int vtrace_v(const typename VtraceAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
   const bool tr = p.trunc != nullptr, pb = p.boot_kind == RLS_BOOT_FULL_ADD;
-  if (!tr && !pb) return launch_tile<VtraceT<T, false, false>, kTileK>(p, g, ws, wsb, s);
-  if (tr && !pb) return launch_tile<VtraceT<T, true, false>, kTileK>(p, g, ws, wsb, s);
-  if (!tr && pb) return launch_tile<VtraceT<T, false, true>, kTileK>(p, g, ws, wsb, s);
-  return launch_tile<VtraceT<T, true, true>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && !pb) return L<VtraceT<T, false, false>>::run(p, g, ws, wsb, s);
+  if (tr && !pb) return L<VtraceT<T, true, false>>::run(p, g, ws, wsb, s);
+  if (!tr && pb) return L<VtraceT<T, false, true>>::run(p, g, ws, wsb, s);
+  return L<VtraceT<T, true, true>>::run(p, g, ws, wsb, s);
 }
-template <class T>
-int lambda_tile(const typename LambdaAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+template <template <class> class L, class T>
+int lambda_v(const typename LambdaAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
   const bool tr = p.trunc != nullptr, pb = p.boot_kind == RLS_BOOT_FULL_ADD && p.boot;
-  if (!tr && !pb) return launch_tile<LambdaT<T, false, false>, kTileK>(p, g, ws, wsb, s);
-  if (tr && !pb) return launch_tile<LambdaT<T, true, false>, kTileK>(p, g, ws, wsb, s);
-  if (!tr && pb) return launch_tile<LambdaT<T, false, true>, kTileK>(p, g, ws, wsb, s);
-  return launch_tile<LambdaT<T, true, true>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && !pb) return L<LambdaT<T, false, false>>::run(p, g, ws, wsb, s);
+  if (tr && !pb) return L<LambdaT<T, true, false>>::run(p, g, ws, wsb, s);
+  if (!tr && pb) return L<LambdaT<T, false, true>>::run(p, g, ws, wsb, s);
+  return L<LambdaT<T, true, true>>::run(p, g, ws, wsb, s);
 }
-template <class T>
-int discounted_tile(const typename DiscountedAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb,
-                    cudaStream_t s) {
+template <template <class> class L, class T>
+int discounted_v(const typename DiscountedAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
   const bool tr = p.trunc != nullptr, pb = p.boot_kind == RLS_BOOT_FULL_ADD && p.boot;
-  if (!tr && !pb) return launch_tile<DiscountedT<T, false, false>, kTileK>(p, g, ws, wsb, s);
-  if (tr && !pb) return launch_tile<DiscountedT<T, true, false>, kTileK>(p, g, ws, wsb, s);
-  if (!tr && pb) return launch_tile<DiscountedT<T, false, true>, kTileK>(p, g, ws, wsb, s);
-  return launch_tile<DiscountedT<T, true, true>, kTileK>(p, g, ws, wsb, s);
+  if (!tr && !pb) return L<DiscountedT<T, false, false>>::run(p, g, ws, wsb, s);
+  if (tr && !pb) return L<DiscountedT<T, true, false>>::run(p, g, ws, wsb, s);
+  if (!tr && pb) return L<DiscountedT<T, false, true>>::run(p, g, ws, wsb, s);
+  return L<DiscountedT<T, true, true>>::run(p, g, ws, wsb, s);
 }
-template <class T>
-int forward_tile(const typename ForwardAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
-  if (p.prev) return launch_tile<ForwardT<T, true>, kTileK>(p, g, ws, wsb, s);
-  return launch_tile<ForwardT<T, false>, kTileK>(p, g, ws, wsb, s);
+template <template <class> class L, class T>
+int forward_v(const typename ForwardAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+  if (p.prev) return L<ForwardT<T, true>>::run(p, g, ws, wsb, s);
+  return L<ForwardT<T, false>>::run(p, g, ws, wsb, s);
+}
+template <template <class> class L, bool B>
+int affine_v(const typename AffineAlg<B>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+  return L<AffineT<B>>::run(p, g, ws, wsb, s);
+}
+
+// Which family serves a call (see path_mode): 3 = tile, 4 = lean rows, else the
+// register kernels behind launch().
+template <class Alg>
+int family(const Geom& g) {
+  const int m = path_mode();
+  const bool rows_ok = g.S % Alg::kVec == 0;
+  if (m == 3) return 3;
+  if (m == 4) return rows_ok ? 4 : 0;
+  if (m != 0) return 0;
+  if (rows_ok && g.N >= kRowsMinEnvs) return 4;
+  return 3;
 }
 
 template <class Alg, int MAXR = 4>
@@ -387,11 +420,19 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
   p.out0 = advantages; p.out1 = nullptr; p.boot_kind = boot_kind; p.gamma = gamma; p.gl = gl;
   if (in_dtype == RLS_F32) {
     GAE_PARAMS(float)
-    if (tile_first<GaeAlg<float>>(g)) return gae_tile<float>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<GaeAlg<float>>(g);
+      if (fam == 3) return gae_v<TileL, float>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return gae_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+    }
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     GAE_PARAMS(__nv_bfloat16)
-    if (tile_first<GaeAlg<__nv_bfloat16>>(g)) return gae_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<GaeAlg<__nv_bfloat16>>(g);
+      if (fam == 3) return gae_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return gae_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+    }
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef GAE_PARAMS
@@ -425,11 +466,19 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
   p.gamma = gamma; p.rho_bar = rho_bar; p.c_bar = c_bar;
   if (in_dtype == RLS_F32) {
     VT_PARAMS(float)
-    if (tile_first<VtraceAlg<float>>(g)) return vtrace_tile<float>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<VtraceAlg<float>>(g);
+      if (fam == 3) return vtrace_v<TileL, float>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return vtrace_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+    }
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
     VT_PARAMS(__nv_bfloat16)
-    if (tile_first<VtraceAlg<__nv_bfloat16>>(g)) return vtrace_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<VtraceAlg<__nv_bfloat16>>(g);
+      if (fam == 3) return vtrace_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return vtrace_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+    }
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef VT_PARAMS
@@ -459,7 +508,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   p.gamma = gamma; p.lam = lambda_; p.c_bar = c_bar; p.rho_bar = rho_bar;
   if (g.M == 0) return RLS_OK;
   const int mode = path_mode();
-  if (tile_first<RetraceAlg>(g)) {
+  if (family<RetraceAlg>(g) == 3) {
     // Stage pi / Qn in the tile ring while a two-stage ring of them fits.
     const int64_t per_step = 8 * num_actions + 28;
     const bool staged = num_actions <= 16 && 2 * per_step * kTileThreads * 9 + 12 * kTileThreads * 9 <= 220 * 1024;
@@ -467,7 +516,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
     if (staged) return launch_tile<RetraceT<true>, 9>(p, g, ws, ws_bytes, s);
     return launch_tile<RetraceT<false>, 9>(p, g, ws, ws_bytes, s);
   }
-  if ((mode == 0 || mode == 1) && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 2>(p, g, s);
+  if ((mode == 0 || mode == 1 || mode == 4) && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 2>(p, g, s);
   // Staging: one warp span of pi and Qn rows plus actions, E and pi_a.
   int rounds = pick_rounds(g.M, 4, 2);
   auto per_warp = [&](int r) {
@@ -508,11 +557,19 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
   p.boot_kind = boot_kind; p.gamma = gamma; p.g1l = gamma * (1.0f - lambda_); p.gl = gamma * lambda_;
   if (in_dtype == RLS_F32) {
     LAM_PARAMS(float)
-    if (tile_first<LambdaAlg<float>>(g)) return lambda_tile<float>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<LambdaAlg<float>>(g);
+      if (fam == 3) return lambda_v<TileL, float>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return lambda_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+    }
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     LAM_PARAMS(__nv_bfloat16)
-    if (tile_first<LambdaAlg<__nv_bfloat16>>(g)) return lambda_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<LambdaAlg<__nv_bfloat16>>(g);
+      if (fam == 3) return lambda_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return lambda_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+    }
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef LAM_PARAMS
@@ -540,11 +597,19 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
   p.boot = (const T*)bootstrap; p.out0 = out; p.out1 = nullptr; p.boot_kind = boot_kind; p.gamma = gamma;
   if (in_dtype == RLS_F32) {
     DISC_PARAMS(float)
-    if (tile_first<DiscountedAlg<float>>(g)) return discounted_tile<float>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<DiscountedAlg<float>>(g);
+      if (fam == 3) return discounted_v<TileL, float>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return discounted_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+    }
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     DISC_PARAMS(__nv_bfloat16)
-    if (tile_first<DiscountedAlg<__nv_bfloat16>>(g)) return discounted_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<DiscountedAlg<__nv_bfloat16>>(g);
+      if (fam == 3) return discounted_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return discounted_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+    }
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef DISC_PARAMS
@@ -567,11 +632,19 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
   p.out0 = out; p.out1 = nullptr; p.k = k; p.prev = prev;
   if (in_dtype == RLS_F32) {
     FWD_PARAMS(float)
-    if (tile_first<ForwardAlg<float>>(g)) return forward_tile<float>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<ForwardAlg<float>>(g);
+      if (fam == 3) return forward_v<TileL, float>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return forward_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+    }
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
     FWD_PARAMS(__nv_bfloat16)
-    if (tile_first<ForwardAlg<__nv_bfloat16>>(g)) return forward_tile<__nv_bfloat16>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<ForwardAlg<__nv_bfloat16>>(g);
+      if (fam == 3) return forward_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return forward_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+    }
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
 #undef FWD_PARAMS
@@ -603,11 +676,19 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
   cudaStream_t s = as_stream(stream);
   if (direction == 0) {
     AffineAlg<true>::Params p{u, v, carry, out, nullptr};
-    if (tile_first<AffineAlg<true>>(g)) return launch_tile<AffineT<true>, kTileK>(p, g, ws, ws_bytes, s);
+    {
+      const int fam = family<AffineAlg<true>>(g);
+      if (fam == 3) return affine_v<TileL, true>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return affine_v<Rows2L, true>(p, g, ws, ws_bytes, s);
+    }
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
   AffineAlg<false>::Params p{u, v, carry, out, nullptr};
-  if (tile_first<AffineAlg<false>>(g)) return launch_tile<AffineT<false>, kTileK>(p, g, ws, ws_bytes, s);
+  {
+      const int fam = family<AffineAlg<false>>(g);
+      if (fam == 3) return affine_v<TileL, false>(p, g, ws, ws_bytes, s);
+      if (fam == 4) return affine_v<Rows2L, false>(p, g, ws, ws_bytes, s);
+    }
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }
 

@@ -131,6 +131,8 @@ struct VtraceT : HomogeneousStreams<InT, 5 + (TR ? 1 : 0) + (PB ? 1 : 0)> {
   static constexpr bool kBackward = true, kNeedsNbr = true, kNextInEmit = false, kEmitReads = true;
   static constexpr int kOuts = 2, kOutSlots = 2, kScratch = 1;
   static constexpr int iLpt = 0, iLpb = 1, iV = 2, iR = 3, iTerm = 4, iTrunc = 5, iBoot = TR ? 6 : 5;
+  // Streams the advantage reads again in pass 2 (all but the log-probs).
+  static constexpr unsigned kEmitMask = ~((1u << iLpt) | (1u << iLpb));
   __host__ __device__ static const void* sptr(const Params& p, int k) {
     switch (k) {
       case iLpt: return p.lpt;
