@@ -481,6 +481,7 @@ def run_b200(args, world, rank, local):
         host = {k: v.to("cpu").pin_memory() for k, v in sets[0].items()}
         h2d = sum(v.numel() * v.element_size() for k, v in host.items() if _used(k, cfg))
         outs_bytes = []
+        pinned_out = []  # results land in pinned host buffers (allocated on the first step)
 
         def e2e_step():
             xd = {k: v.to(dev, non_blocking=True) for k, v in host.items() if _used(k, cfg)}
@@ -488,10 +489,12 @@ def run_b200(args, world, rank, local):
             for f in make_calls(cfg, xd, split).values():
                 r = f()
                 res.extend(r if isinstance(r, tuple) else (r,))
-            outs = [r.to("cpu", non_blocking=True) for r in res]
-            if not outs_bytes:
-                outs_bytes.append(sum(o.numel() * o.element_size() for o in outs))
-            return outs
+            if not pinned_out:
+                pinned_out.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
+                outs_bytes.append(sum(o.numel() * o.element_size() for o in pinned_out))
+            for o, r in zip(pinned_out, res):
+                o.copy_(r, non_blocking=True)
+            return pinned_out
 
         with torch.cuda.stream(stream):
             for _ in range(2):
@@ -547,6 +550,8 @@ def run_b200(args, world, rank, local):
 
 def run_ncu(args, local):
     cfg = CONFIGS[args.config]
+    if args.envs:
+        cfg = dict(cfg, N=args.envs)
     dev = torch.device("cuda", local)
     x = make_inputs(cfg, dev, seed=1)
     calls = make_calls(cfg, x)
@@ -588,6 +593,7 @@ def main():
                     help="profiling mode for ncu: W warm-up rounds then K rounds of one eager launch per "
                          "function, in --config order; no timing, no graphs, prints nothing")
     ap.add_argument("--only", default="", help="comma list of functions to run (default: all of the config)")
+    ap.add_argument("--envs", type=int, default=0, help="--ncu mode: override num_envs (a smaller slice to profile)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
