@@ -55,6 +55,7 @@ static_assert(sizeof(WsHeader) == 64, "header is 64 bytes");
 
 constexpr unsigned kFlagAgg = 1u;   // aggregate of the tile published
 constexpr unsigned kFlagIncl = 2u;  // inclusive prefix of the tile published
+constexpr unsigned kFlagSelf = 3u;  // inclusive prefix that needed no carry (product of b is 0)
 constexpr unsigned kEpochMask = 0x3fffffffu;
 
 struct Workspace {

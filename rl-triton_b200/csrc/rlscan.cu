@@ -110,10 +110,11 @@ int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
 }
 
 // ---- kernel family ----------------------------------------------------------
-// RLS_PATH=auto (default) | rows2 | rows | flat | tile.  auto: the lean row
-// kernel (rows2) when every row starts 16-byte aligned and there are enough
-// rows to fill the GPU (one warp per row, no workspace, no barrier), else the
-// TMA-staged tile kernel, which also parallelises along time.  The others
+// RLS_PATH=auto (default) | rows2 | flat2 | rows | flat | tile.  auto: the lean
+// row kernel (rows2) when every row starts 16-byte aligned and there are enough
+// rows to fill the GPU (one warp per row, no workspace, no barrier); else, for
+// aligned rows, flat2 (one warp per 512-step tile with a look-back, which also
+// parallelises along time); else the TMA-staged tile kernel.  The others
 // force one family (the row kernels fall back to flat when rows are not
 // aligned); rows is the first row kernel with generic policies, kept as a
 // cross-check and for Retrace.
@@ -124,6 +125,7 @@ int path_mode() {
   if (!std::strcmp(s, "flat")) return 2;
   if (!std::strcmp(s, "tile")) return 3;
   if (!std::strcmp(s, "rows2")) return 4;
+  if (!std::strcmp(s, "flat2")) return 5;
   return 0;
 }
 
@@ -252,6 +254,25 @@ struct Rows2L {
   }
 };
 
+template <class P>
+struct Flat2L {
+  static int run(const typename P::Params& p, const Geom& g0, void* ws, size_t wsb, cudaStream_t s) {
+    constexpr int R = sizeof(typename P::InT) == 4 ? 4 : 2;  // 512-element tiles
+    constexpr int64_t CH = 32LL * R * (16 / (int)sizeof(typename P::InT));
+    Geom g = g0;
+    g.num_tiles = (g.M + CH - 1) / CH;
+    if (g.num_tiles == 0) return RLS_OK;
+    if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
+    g.ws_cap = ws ? ws_capacity(wsb) : 0;
+    if (g.ws_cap < g.num_tiles) return RLS_EWORKSPACE;
+    // Same convention as the other look-back kernels: a launch uses the current
+    // epoch and leaves the next one for the following launch on this workspace.
+    flat2_kernel<P, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
+    advance_epoch<<<1, 1, 0, s>>>(ws);
+    return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  }
+};
+
 // Compile-time variant dispatch (truncations present, per-step bootstrap kind).
 template <template <class> class L, class T>
 int gae_v(const typename GaeAlg<T>::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
@@ -305,9 +326,10 @@ int family(const Geom& g) {
   const bool rows_ok = g.S % Alg::kVec == 0;
   if (m == 3) return 3;
   if (m == 4) return rows_ok ? 4 : 0;
+  if (m == 5) return rows_ok ? 5 : 3;
   if (m != 0) return 0;
   if (rows_ok && g.N >= kRowsMinEnvs) return 4;
-  return 3;
+  return rows_ok ? 5 : 3;
 }
 
 template <class Alg, int MAXR = 4>
@@ -424,6 +446,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       const int fam = family<GaeAlg<float>>(g);
       if (fam == 3) return gae_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return gae_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return gae_v<Flat2L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -432,6 +455,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       const int fam = family<GaeAlg<__nv_bfloat16>>(g);
       if (fam == 3) return gae_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return gae_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return gae_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -470,6 +494,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       const int fam = family<VtraceAlg<float>>(g);
       if (fam == 3) return vtrace_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return vtrace_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return vtrace_v<Flat2L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
@@ -478,6 +503,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       const int fam = family<VtraceAlg<__nv_bfloat16>>(g);
       if (fam == 3) return vtrace_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return vtrace_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return vtrace_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -508,7 +534,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   p.gamma = gamma; p.lam = lambda_; p.c_bar = c_bar; p.rho_bar = rho_bar;
   if (g.M == 0) return RLS_OK;
   const int mode = path_mode();
-  if (family<RetraceAlg>(g) == 3) {
+  if (family<RetraceAlg>(g) == 3 || family<RetraceAlg>(g) == 5) {
     // Stage pi / Qn in the tile ring while a two-stage ring of them fits.
     const int64_t per_step = 8 * num_actions + 28;
     const bool staged = num_actions <= 16 && 2 * per_step * kTileThreads * 9 + 12 * kTileThreads * 9 <= 220 * 1024;
@@ -561,6 +587,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       const int fam = family<LambdaAlg<float>>(g);
       if (fam == 3) return lambda_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return lambda_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return lambda_v<Flat2L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -569,6 +596,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       const int fam = family<LambdaAlg<__nv_bfloat16>>(g);
       if (fam == 3) return lambda_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return lambda_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return lambda_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -601,6 +629,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       const int fam = family<DiscountedAlg<float>>(g);
       if (fam == 3) return discounted_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return discounted_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return discounted_v<Flat2L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -609,6 +638,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       const int fam = family<DiscountedAlg<__nv_bfloat16>>(g);
       if (fam == 3) return discounted_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return discounted_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return discounted_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -636,6 +666,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       const int fam = family<ForwardAlg<float>>(g);
       if (fam == 3) return forward_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return forward_v<Rows2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return forward_v<Flat2L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -644,6 +675,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       const int fam = family<ForwardAlg<__nv_bfloat16>>(g);
       if (fam == 3) return forward_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return forward_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return forward_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -680,6 +712,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       const int fam = family<AffineAlg<true>>(g);
       if (fam == 3) return affine_v<TileL, true>(p, g, ws, ws_bytes, s);
       if (fam == 4) return affine_v<Rows2L, true>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return affine_v<Flat2L, true>(p, g, ws, ws_bytes, s);
     }
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
@@ -688,6 +721,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       const int fam = family<AffineAlg<false>>(g);
       if (fam == 3) return affine_v<TileL, false>(p, g, ws, ws_bytes, s);
       if (fam == 4) return affine_v<Rows2L, false>(p, g, ws, ws_bytes, s);
+      if (fam == 5) return affine_v<Flat2L, false>(p, g, ws, ws_bytes, s);
     }
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }

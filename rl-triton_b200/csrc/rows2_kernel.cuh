@@ -60,143 +60,173 @@ __device__ __forceinline__ void rows2_unpack(const Rows2Chunk<P, R>& ch, int r,
   }
 }
 
-// Scan one chunk with the carry entering it; returns the carry leaving it.
+// One chunk (R rounds x 32 lanes x VEC elements) in registers: pass 1 builds
+// the element maps and the shuffle scans, pass 2 emits from the carry.  Lane
+// l's vector of round r starts at flat index i0[r] = (row, col0[r]).
 template <class P, int R>
-__device__ __forceinline__ float rows2_chunk(const typename P::Params& p, const Geom& g, int64_t row,
-                                             int64_t rbase, int64_t cbase, int lane, const Rows2Chunk<P, R>& ch,
-                                             float carry, typename P::Nbr& edge_nbr) {
+struct ChunkScan {
   using Nbr = typename P::Nbr;
-  constexpr int VEC = Rows2Chunk<P, R>::VEC;
-  constexpr int NI = P::kNI;
-  constexpr bool BWD = P::kBackward;
-  constexpr int JE = BWD ? VEC - 1 : 0;
-  const int64_t S = g.S;
-  const int glob = g.edge_global;
-
-  int64_t col0[R];
+  static constexpr int VEC = Rows2Chunk<P, R>::VEC;
+  static constexpr int NI = P::kNI;
+  static constexpr bool BWD = P::kBackward;
+  static constexpr int JE = BWD ? VEC - 1 : 0;
+  int64_t i0[R], row[R], col0[R];
   bool valid[R], edge_v[R];
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    col0[r] = cbase + (int64_t)r * 32 * VEC + lane * VEC;
-    valid[r] = col0[r] < S;
-    edge_v[r] = valid[r] && (BWD ? (col0[r] + VEC == S) : (col0[r] == 0));
-  }
-
-  // Neighbour entering each lane's vector (backward: the element after it).
   Nbr nbe[R];
-  if constexpr (P::kNeedsNbr) {
-    Nbr own[R];
+  float ca[R][VEC], cb[R][VEC], scr[R][VEC];
+  Pair excl[R], tot[R];
+
+  // edge_nbr: the neighbour across the chunk's carry-entry edge (element after
+  // the chunk backward, before it forward); returns the one the next chunk in
+  // walk order needs from this chunk.
+  __device__ __forceinline__ Nbr pass1(const typename P::Params& p, const Geom& g, int lane,
+                                       const Rows2Chunk<P, R>& ch, Nbr edge_nbr) {
+    const int glob = g.edge_global;
+    if constexpr (P::kNeedsNbr) {
+      Nbr own[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float in[NI][VEC];
+        rows2_unpack<P, R>(ch, r, in);
+        own[r] = P::template nbr_of<VEC>(in, BWD ? 0 : VEC - 1);
+      }
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if constexpr (BWD) {
+          Nbr h = shfl_down_any(own[r], 1);
+          const Nbr w = (r + 1 < R) ? shfl_idx_any(own[(r + 1) % R], 0) : edge_nbr;
+          if (lane == 31) h = w;
+          nbe[r] = h;
+        } else {
+          Nbr h = shfl_up_any(own[r], 1);
+          const Nbr w = (r > 0) ? shfl_idx_any(own[(r + R - 1) % R], 31) : edge_nbr;
+          if (lane == 0) h = w;
+          nbe[r] = h;
+        }
+      }
+      edge_nbr = BWD ? shfl_idx_any(own[0], 0) : shfl_idx_any(own[R - 1], 31);
+    }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       float in[NI][VEC];
       rows2_unpack<P, R>(ch, r, in);
-      own[r] = P::template nbr_of<VEC>(in, BWD ? 0 : VEC - 1);
+      const EdgeLoc L{i0[r], row[r], col0[r], g.S, glob};
+      Nbr nb{};
+      if constexpr (P::kNeedsNbr) nb = nbe[r];
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) {
+        const int e = BWD ? (VEC - 1 - q) : q;
+        P::template coeff<VEC>(p, in, e, nb, (e == JE) && edge_v[r], L, e, &scr[r][e], ca[r][e], cb[r][e]);
+        if constexpr (P::kNeedsNbr) nb = P::template nbr_of<VEC>(in, e);
+      }
+      if (!valid[r]) {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) { ca[r][e] = 0.f; cb[r][e] = 1.f; }
+      }
+      Pair m = pair_identity();
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) {
+        const int e = BWD ? (VEC - 1 - q) : q;
+        m = compose(Pair{ca[r][e], cb[r][e]}, m);
+      }
+      Pair incl = m;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        if constexpr (BWD) {
+          const Pair o = shfl_pair_down(incl, d);
+          if (lane + d < 32) incl = compose(incl, o);
+        } else {
+          const Pair o = shfl_pair_up(incl, d);
+          if (lane >= d) incl = compose(incl, o);
+        }
+      }
+      if constexpr (BWD) {
+        const Pair x = shfl_pair_down(incl, 1);
+        excl[r] = (lane == 31) ? pair_identity() : x;
+        tot[r] = shfl_pair_idx(incl, 0);
+      } else {
+        const Pair x = shfl_pair_up(incl, 1);
+        excl[r] = (lane == 0) ? pair_identity() : x;
+        tot[r] = shfl_pair_idx(incl, 31);
+      }
+    }
+    return edge_nbr;
+  }
+
+  // The chunk's composed map (carry entering -> state leaving).
+  __device__ __forceinline__ Pair aggregate() const {
+    Pair agg = pair_identity();
+    if constexpr (BWD) {
+#pragma unroll
+      for (int r = R - 1; r >= 0; --r) agg = compose(tot[r], agg);
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) agg = compose(tot[r], agg);
+    }
+    return agg;
+  }
+
+  // Emit and store with the carry entering the chunk; returns the carry leaving it.
+  __device__ __forceinline__ float pass2(const typename P::Params& p, const Geom& g, const Rows2Chunk<P, R>& ch,
+                                         float carry) {
+    const int glob = g.edge_global;
+    float cr[R];
+    float c = carry;
+    if constexpr (BWD) {
+#pragma unroll
+      for (int r = R - 1; r >= 0; --r) { cr[r] = c; c = apply(tot[r], c); }
+    } else {
+#pragma unroll
+      for (int r = 0; r < R; ++r) { cr[r] = c; c = apply(tot[r], c); }
     }
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      if constexpr (BWD) {
-        Nbr h = shfl_down_any(own[r], 1);
-        const Nbr w = (r + 1 < R) ? shfl_idx_any(own[(r + 1) % R], 0) : edge_nbr;
-        if (lane == 31) h = w;
-        nbe[r] = h;
-      } else {
-        Nbr h = shfl_up_any(own[r], 1);
-        const Nbr w = (r > 0) ? shfl_idx_any(own[(r + R - 1) % R], 31) : edge_nbr;
-        if (lane == 0) h = w;
-        nbe[r] = h;
+      float in[NI][VEC];
+      if constexpr (P::kEmitReads) rows2_unpack<P, R>(ch, r, in, P::kEmitMask);
+      const EdgeLoc L{i0[r], row[r], col0[r], g.S, glob};
+      float x = apply(excl[r], cr[r]);
+      float o0[VEC], o1[VEC];
+      Nbr nb{};
+      if constexpr (P::kNeedsNbr) nb = nbe[r];
+#pragma unroll
+      for (int q = 0; q < VEC; ++q) {
+        const int e = BWD ? (VEC - 1 - q) : q;
+        const float xo = x;
+        x = fmaf(cb[r][e], x, ca[r][e]);
+        P::template emit<VEC>(p, in, e, x, xo, nb, (e == JE) && edge_v[r], L, e, &scr[r][e], o0[e], o1[e]);
+        if constexpr (P::kNeedsNbr && P::kEmitReads) nb = P::template nbr_of<VEC>(in, e);
+      }
+      if (valid[r]) {
+#pragma unroll
+        for (int q = 0; q < VEC; q += 4) {
+          st_stream_f4(p.out0 + i0[r] + q, make_float4(o0[q], o0[q + 1], o0[q + 2], o0[q + 3]));
+          if constexpr (P::kOuts > 1)
+            st_stream_f4(p.out1 + i0[r] + q, make_float4(o1[q], o1[q + 1], o1[q + 2], o1[q + 3]));
+        }
       }
     }
-    edge_nbr = BWD ? shfl_idx_any(own[0], 0) : shfl_idx_any(own[R - 1], 31);
+    return c;
   }
+};
 
-  // Pass 1: coefficients, lane maps, shuffle scan per round.
-  float ca[R][VEC], cb[R][VEC], scr[R][VEC];
-  Pair excl[R], tot[R];
+// Scan one chunk of one row with the carry entering it; returns the carry leaving it.
+template <class P, int R>
+__device__ __forceinline__ float rows2_chunk(const typename P::Params& p, const Geom& g, int64_t row,
+                                             int64_t rbase, int64_t cbase, int lane, const Rows2Chunk<P, R>& ch,
+                                             float carry, typename P::Nbr& edge_nbr) {
+  constexpr int VEC = Rows2Chunk<P, R>::VEC;
+  constexpr bool BWD = P::kBackward;
+  ChunkScan<P, R> cs;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    float in[NI][VEC];
-    rows2_unpack<P, R>(ch, r, in);
-    const EdgeLoc L{rbase + col0[r], row, col0[r], S, glob};
-    Nbr nb{};
-    if constexpr (P::kNeedsNbr) nb = nbe[r];
-#pragma unroll
-    for (int q = 0; q < VEC; ++q) {
-      const int e = BWD ? (VEC - 1 - q) : q;
-      P::template coeff<VEC>(p, in, e, nb, (e == JE) && edge_v[r], L, e, &scr[r][e], ca[r][e], cb[r][e]);
-      if constexpr (P::kNeedsNbr) nb = P::template nbr_of<VEC>(in, e);
-    }
-    if (!valid[r]) {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) { ca[r][e] = 0.f; cb[r][e] = 1.f; }
-    }
-    Pair m = pair_identity();
-#pragma unroll
-    for (int q = 0; q < VEC; ++q) {
-      const int e = BWD ? (VEC - 1 - q) : q;
-      m = compose(Pair{ca[r][e], cb[r][e]}, m);
-    }
-    Pair incl = m;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      if constexpr (BWD) {
-        const Pair o = shfl_pair_down(incl, d);
-        if (lane + d < 32) incl = compose(incl, o);
-      } else {
-        const Pair o = shfl_pair_up(incl, d);
-        if (lane >= d) incl = compose(incl, o);
-      }
-    }
-    if constexpr (BWD) {
-      const Pair x = shfl_pair_down(incl, 1);
-      excl[r] = (lane == 31) ? pair_identity() : x;
-      tot[r] = shfl_pair_idx(incl, 0);
-    } else {
-      const Pair x = shfl_pair_up(incl, 1);
-      excl[r] = (lane == 0) ? pair_identity() : x;
-      tot[r] = shfl_pair_idx(incl, 31);
-    }
+    cs.col0[r] = cbase + (int64_t)r * 32 * VEC + lane * VEC;
+    cs.row[r] = row;
+    cs.i0[r] = rbase + cs.col0[r];
+    cs.valid[r] = cs.col0[r] < g.S;
+    cs.edge_v[r] = cs.valid[r] && (BWD ? (cs.col0[r] + VEC == g.S) : (cs.col0[r] == 0));
   }
-
-  // Round carries from the chunk's carry-entry edge inward.
-  float cr[R];
-  float c = carry;
-  if constexpr (BWD) {
-#pragma unroll
-    for (int r = R - 1; r >= 0; --r) { cr[r] = c; c = apply(tot[r], c); }
-  } else {
-#pragma unroll
-    for (int r = 0; r < R; ++r) { cr[r] = c; c = apply(tot[r], c); }
-  }
-
-  // Pass 2: emit and store.
-#pragma unroll
-  for (int r = 0; r < R; ++r) {
-    float in[NI][VEC];
-    if constexpr (P::kEmitReads) rows2_unpack<P, R>(ch, r, in, P::kEmitMask);
-    const EdgeLoc L{rbase + col0[r], row, col0[r], S, glob};
-    float x = apply(excl[r], cr[r]);
-    float o0[VEC], o1[VEC];
-    Nbr nb{};
-    if constexpr (P::kNeedsNbr) nb = nbe[r];
-#pragma unroll
-    for (int q = 0; q < VEC; ++q) {
-      const int e = BWD ? (VEC - 1 - q) : q;
-      const float xo = x;
-      x = fmaf(cb[r][e], x, ca[r][e]);
-      P::template emit<VEC>(p, in, e, x, xo, nb, (e == JE) && edge_v[r], L, e, &scr[r][e], o0[e], o1[e]);
-      if constexpr (P::kNeedsNbr && P::kEmitReads) nb = P::template nbr_of<VEC>(in, e);
-    }
-    if (valid[r]) {
-      const int64_t i0 = rbase + col0[r];
-#pragma unroll
-      for (int q = 0; q < VEC; q += 4) {
-        st_stream_f4(p.out0 + i0 + q, make_float4(o0[q], o0[q + 1], o0[q + 2], o0[q + 3]));
-        if constexpr (P::kOuts > 1)
-          st_stream_f4(p.out1 + i0 + q, make_float4(o1[q], o1[q + 1], o1[q + 2], o1[q + 3]));
-      }
-    }
-  }
-  return c;
+  edge_nbr = cs.pass1(p, g, lane, ch, edge_nbr);
+  return cs.pass2(p, g, ch, carry);
 }
 
 template <class P, int WPB, int R>
@@ -223,6 +253,184 @@ __global__ void __launch_bounds__(WPB * 32) rows2_kernel(const typename P::Param
     if (k + 2 < nch) rows2_load<P, R>(p, rbase, S, cb_of(k + 2), lane, a);
     carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k + 1), lane, b, carry, edge_nbr);
   }
+}
+
+}  // namespace rls
+
+namespace rls {
+
+// ===========================================================================
+// flat2: one warp per 512-element tile of the flat [N*S] array, for few long
+// rows.  Each warp loads its tile straight into registers (the ChunkScan of the
+// row kernel), publishes the tile's map, takes its carry from a decoupled
+// look-back over the preceding tiles, and emits.  Tile t is scanned by warp
+// t % 4 of block t / 4 (blocks start in index order; every wait is bounded
+// anyway and latches an error bit instead of hanging).  A launch uses the
+// workspace's current epoch, like the other look-back kernels, and a one-thread
+// kernel launched right after it advances the epoch, so blocks need no exit
+// counter.
+// ===========================================================================
+
+__global__ void advance_epoch(void* ws_base) {
+  WsHeader* h = reinterpret_cast<WsHeader*>(ws_base);
+  h->epoch = (h->epoch + 1u) & kEpochMask;
+}
+
+// Carry entering tile `ticket` (the state after tile ticket-1), read from the
+// tiles published before it, 32 at a time (lane l reads tile ticket-1-32w-l).
+// A tile publishes its map (kFlagAgg), its exact inclusive value when the map
+// does not depend on the carry (kFlagSelf), and its inclusive value once its
+// own look-back is done (kFlagIncl).  The carry is the serial fold
+// c <- a_m + b_m * c from a stop point that depends only on the data, so the
+// outputs are bit-identical from run to run:
+//  * decaying recurrences: the nearest kFlagSelf tile, or the nearest tile where
+//    the running product of b's (taken from ticket-1 backwards) is exactly 0 --
+//    the fold starts from 0 there; for gamma*lambda decays this comes within a
+//    few tiles;
+//  * running sums (b only 0 or 1, `unit`): the nearest tile with any inclusive
+//    value -- each is the same serial fold, so whichever is found first gives
+//    the same result.
+// Without a stop within kLookWindows windows, the predecessor's own inclusive
+// value (computed by the same rule) is awaited instead.
+constexpr int kLookWindows = 4;
+__device__ __forceinline__ float flat2_look_back(const Workspace& ws, int64_t ticket, unsigned tag, int lane,
+                                                 bool unit, unsigned& err) {
+  constexpr unsigned FULL = 0xffffffffu;
+  float As[kLookWindows], Bs[kLookWindows];
+  float cum = 1.f;
+  float c = 0.f;
+  bool found = false;
+#pragma unroll
+  for (int w = 0; w < kLookWindows; ++w) {
+    if (found) break;
+    const int64_t pj = ticket - 1 - 32 * w - lane;
+    unsigned kind = kFlagSelf;
+    float a = 0.f, b = 0.f, inc = 0.f;
+    if (pj >= 0) {
+      unsigned f = 0, it = 0;
+      while (true) {
+        f = ld_acquire_u32(&ws.flags[pj]);
+        if ((f & ~3u) == (tag & ~3u) && (f & 3u)) break;
+        if (++it > kSpinLimit) { err |= 1u; f = tag | kFlagSelf; break; }
+        if (it > 8) __nanosleep(32);
+      }
+      kind = f & 3u;
+      if (kind == kFlagSelf) {
+        inc = __ldcg(&ws.incl[pj]).x;
+        a = inc;
+      } else {
+        const float2 v = __ldcg(&ws.agg[pj]);
+        a = v.x;
+        b = v.y;
+        if (unit && kind == kFlagIncl) inc = __ldcg(&ws.incl[pj]).x;
+      }
+    }
+    float pr = b;  // running product of b, nearest tile first
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float o = __shfl_up_sync(FULL, pr, d);
+      if (lane >= d) pr *= o;
+    }
+    pr *= cum;
+    const bool stop = (kind == kFlagSelf) || (unit ? (kind == kFlagIncl) : (pr == 0.f));
+    const unsigned m = __ballot_sync(FULL, stop);
+    if (m) {
+      const int st = __ffs(m) - 1;
+      const unsigned ks = __shfl_sync(FULL, kind, st);
+      int l0;
+      if (ks == kFlagSelf || (unit && ks == kFlagIncl)) {
+        c = __shfl_sync(FULL, inc, st);
+        l0 = st - 1;
+      } else {
+        c = 0.f;
+        l0 = st;
+      }
+      for (int l = l0; l >= 0; --l) c = fmaf(__shfl_sync(FULL, b, l), c, __shfl_sync(FULL, a, l));
+#pragma unroll
+      for (int u = w - 1; u >= 0; --u)
+        for (int l = 31; l >= 0; --l) c = fmaf(__shfl_sync(FULL, Bs[u], l), c, __shfl_sync(FULL, As[u], l));
+      found = true;
+    } else {
+      As[w] = a;
+      Bs[w] = b;
+      cum = __shfl_sync(FULL, pr, 31);
+    }
+  }
+  if (!found) {
+    float v = 0.f;
+    if (lane == 0) {
+      unsigned it = 0;
+      while (true) {
+        const unsigned f = ld_acquire_u32(&ws.flags[ticket - 1]);
+        if ((f & ~3u) == (tag & ~3u) && (f & 3u) >= kFlagIncl) { v = __ldcg(&ws.incl[ticket - 1]).x; break; }
+        if (++it > kSpinLimit) { err |= 1u; break; }
+        __nanosleep(64);
+      }
+    }
+    c = __shfl_sync(FULL, v, 0);
+  }
+  return c;
+}
+
+template <class P, int R>
+__global__ void __launch_bounds__(128) flat2_kernel(const typename P::Params p, const Geom g, void* ws_base) {
+  using CS = ChunkScan<P, R>;
+  constexpr int VEC = CS::VEC;
+  constexpr int64_t CH = (int64_t)R * 32 * VEC;
+  constexpr bool BWD = P::kBackward;
+  constexpr unsigned FULL = 0xffffffffu;
+  __shared__ unsigned s_epoch;
+  const Workspace ws = ws_carve(ws_base, g.ws_cap);
+  if (threadIdx.x == 0) s_epoch = ld_relaxed_u32(&ws.hdr->epoch);
+  __syncthreads();
+  const unsigned tag = s_epoch << 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t ticket = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (ticket >= g.num_tiles) return;
+  const int64_t tile = BWD ? (g.num_tiles - 1 - ticket) : ticket;
+  const int64_t base = tile * CH;
+  unsigned err = 0;
+
+  Rows2Chunk<P, R> ch;
+  rows2_load<P, R>(p, 0, g.M, base, lane, ch);
+  CS cs;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    cs.i0[r] = base + (int64_t)r * 32 * VEC + lane * VEC;
+    cs.valid[r] = cs.i0[r] < g.M;
+    row_col(cs.i0[r], g.S, cs.row[r], cs.col0[r]);
+    cs.edge_v[r] = cs.valid[r] && (BWD ? (cs.col0[r] + VEC == g.S) : (cs.col0[r] == 0));
+  }
+  typename P::Nbr nb{};
+  if constexpr (P::kNeedsNbr) {
+    const int64_t gn = BWD ? base + CH : base - 1;
+    if (BWD ? (gn < g.M) : (gn >= 0)) nb = P::nbr_global(p, gn);
+  }
+  cs.pass1(p, g, lane, ch, nb);
+  const Pair agg = cs.aggregate();
+  if (lane == 0) {
+    if (agg.b == 0.f || ticket == 0) {
+      __stcg(&ws.incl[ticket], make_float2(agg.a, 0.f));
+      st_release_u32(&ws.flags[ticket], tag | kFlagSelf);
+    } else {
+      __stcg(&ws.agg[ticket], make_float2(agg.a, agg.b));
+      st_release_u32(&ws.flags[ticket], tag | kFlagAgg);
+    }
+  }
+  // The tile's entry element: backward the last lane's last element of the last round.
+  const int rent = BWD ? R - 1 : 0;
+  const bool keep = P::kNextInEmit ? !cs.edge_v[rent] : (cs.cb[rent][CS::JE] != 0.f);
+  const bool need = ticket > 0 && __shfl_sync(FULL, keep ? 1 : 0, BWD ? 31 : 0);
+  float carry = 0.f;
+  if (need) {
+    carry = flat2_look_back(ws, ticket, tag, lane, P::unit_decay(p), err);
+    if (lane == 0 && agg.b != 0.f) {
+      __stcg(&ws.incl[ticket], make_float2(apply(agg, carry), 0.f));
+      st_release_u32(&ws.flags[ticket], tag | kFlagIncl);
+    }
+  }
+  cs.pass2(p, g, ch, carry);
+  if (err && lane == 0) atomicOr(&ws.hdr->error, err);
 }
 
 }  // namespace rls

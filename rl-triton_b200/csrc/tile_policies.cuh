@@ -34,6 +34,10 @@ struct HomogeneousStreams {
   static constexpr int kNS = NSTREAMS;
   static constexpr int kNI = NSTREAMS;
   static constexpr bool kElemLoad = false;
+  // Decays that are only ever 0 or 1 (running sums): the flat2 look-back may
+  // stop at any published inclusive value.
+  template <class Params>
+  __device__ __forceinline__ static bool unit_decay(const Params&) { return false; }
   template <int K>
   __host__ __device__ static constexpr int vec() { return (K % vec_of<InT>() == 0) ? vec_of<InT>() : 1; }
   template <class Params>
@@ -430,6 +434,7 @@ struct ForwardT : HomogeneousStreams<InT, 2> {
   using Params = typename ForwardAlg<InT>::Params;
   using Nbr = float;
   static constexpr bool kBackward = false, kNeedsNbr = PREV, kNextInEmit = false, kEmitReads = false;
+  __device__ __forceinline__ static bool unit_decay(const Params& p) { return p.k == 1.f; }
   static constexpr int kOuts = 1, kOutSlots = 1, kScratch = 0;
   __host__ __device__ static const void* sptr(const Params& p, int k) { return k == 0 ? (const void*)p.x : p.done; }
   template <int VEC>
@@ -468,6 +473,7 @@ struct AffineT : HomogeneousStreams<float, 2> {
   using Params = typename AffineAlg<BWD>::Params;
   using Nbr = float;
   static constexpr bool kBackward = BWD, kNeedsNbr = false, kNextInEmit = false, kEmitReads = false;
+  __device__ __forceinline__ static bool unit_decay(const Params&) { return true; }
   static constexpr int kOuts = 1, kOutSlots = 1, kScratch = 0;
   __host__ __device__ static const void* sptr(const Params& p, int k) { return k == 0 ? p.u : p.v; }
   template <int VEC>

@@ -33,7 +33,7 @@ def T(a, dev="cuda", dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)
 
 
-@pytest.fixture(autouse=True, params=["auto", "rows2", "tile", "rows", "flat"])
+@pytest.fixture(autouse=True, params=["auto", "rows2", "flat2", "tile", "rows", "flat"])
 def kernel_path(request, monkeypatch):
     """Run every case on each kernel family: the library's own choice ("auto"),
     the TMA-staged tile kernel, the row-parallel register kernel (one warp per
@@ -313,3 +313,26 @@ def test_lambda1_gae_is_monte_carlo():
     got = rl_triton.compute_gae(T(r), T(v), T(np.zeros((n, t), np.float32)), gamma=gamma, lambda_=1.0,
                                 last_value=T(lv))
     close(got.cpu().numpy(), ret - v, rtol=1e-4, atol=1e-4)
+
+
+def test_kernel_families_share_one_workspace():
+    """Every look-back kernel family leaves the per-stream workspace ready for the
+    next launch of any family (each launch runs under a fresh epoch)."""
+    import os
+    import rl_triton
+    from rl_triton import _native as nat
+    old = os.environ.get("RLS_PATH")
+    try:
+        for path in ["flat2", "tile", "flat", "flat2", "flat", "tile", "flat2"]:
+            os.environ["RLS_PATH"] = path
+            for n, t in [(64, 512), (1, 4095), (3, 5000)]:
+                x = rng_inputs(n, t, seed=n + t)
+                got = rl_triton.compute_gae(T(x["r"]), T(x["v"]), T(x["term"])).cpu().numpy()
+                close(got, orc.gae(x["r"], x["v"], x["term"]), msg=f"{path} {n}x{t}")
+                torch.cuda.synchronize()
+                assert nat.workspace_error() == 0, f"{path} {n}x{t}"
+    finally:
+        if old is None:
+            os.environ.pop("RLS_PATH", None)
+        else:
+            os.environ["RLS_PATH"] = old
