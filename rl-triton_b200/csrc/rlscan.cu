@@ -20,7 +20,7 @@ using namespace rls;
 namespace {
 
 constexpr int kWarps = 4;
-constexpr int64_t kMinTileElems = kWarps * 1 * 32 * 4;  // smallest tile of any launch
+constexpr int64_t kMinTileElems = 128;  // smallest tile of any launch (a one-round fp32 flat2 tile)
 
 inline bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15u) == 0; }
 
@@ -110,11 +110,13 @@ int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
 }
 
 // ---- kernel family ----------------------------------------------------------
-// RLS_PATH=auto (default) | rows2 | flat2 | rows | flat | tile.  auto: the lean
-// row kernel (rows2) when every row starts 16-byte aligned and there are enough
-// rows to fill the GPU (one warp per row, no workspace, no barrier); else, for
-// aligned rows, flat2 (one warp per 512-step tile with a look-back, which also
-// parallelises along time); else the TMA-staged tile kernel.  The others
+// RLS_PATH=auto (default) | rows2 | flat3 | flat2 | rows | flat | tile.  auto:
+// the lean row kernel (rows2) when every row starts 16-byte aligned and there
+// are enough rows to fill the GPU (one warp per row, no workspace, no barrier);
+// else, for aligned rows, flat3 (one warp per 2048-step super-tile walked twice
+// around one look-back, which also parallelises along time); else the
+// TMA-staged tile kernel.  flat2 is flat3's one-walk predecessor (one warp per
+// 512-step tile).  The others
 // force one family (the row kernels fall back to flat when rows are not
 // aligned); rows is the first row kernel with generic policies, kept as a
 // cross-check and for Retrace.
@@ -126,6 +128,7 @@ int path_mode() {
   if (!std::strcmp(s, "tile")) return 3;
   if (!std::strcmp(s, "rows2")) return 4;
   if (!std::strcmp(s, "flat2")) return 5;
+  if (!std::strcmp(s, "flat3")) return 6;
   return 0;
 }
 
@@ -254,22 +257,66 @@ struct Rows2L {
   }
 };
 
+template <class P, int R>
+int launch_flat2(const typename P::Params& p, const Geom& g0, void* ws, size_t wsb, cudaStream_t s) {
+  constexpr int64_t CH = 32LL * R * (16 / (int)sizeof(typename P::InT));
+  Geom g = g0;
+  g.num_tiles = (g.M + CH - 1) / CH;
+  if (g.num_tiles == 0) return RLS_OK;
+  if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
+  g.ws_cap = ws ? packed_capacity(wsb) : 0;
+  // A workspace sized for fewer, larger tiles (e.g. the fixed scratch of
+  // rls_gae_noalloc) may be too small for flat2's records: the tile kernel
+  // then serves the call.
+  if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
+  // Same convention as the other look-back kernels: a launch uses the current
+  // epoch and leaves the next one for the following launch on this workspace.
+  flat2_kernel<P, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
+  advance_epoch<<<1, 1, 0, s>>>(ws);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+}
+
+template <class P, int NCH, int R>
+int launch_flat3(const typename P::Params& p, const Geom& g0, void* ws, size_t wsb, cudaStream_t s) {
+  constexpr int64_t ST = 32LL * NCH * R * (16 / (int)sizeof(typename P::InT));
+  Geom g = g0;
+  g.num_tiles = (g.M + ST - 1) / ST;
+  if (g.num_tiles == 0) return RLS_OK;
+  if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
+  g.ws_cap = ws ? packed_capacity(wsb) : 0;
+  if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
+  flat3_kernel<P, NCH, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
+  advance_epoch<<<1, 1, 0, s>>>(ws);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+}
+
+// Super-tiles of RLS_FLAT3_STEPS steps (1024, 2048, 4096; default 2048) in
+// chunks of one 16-byte vector per lane (two vectors per lane measured slower:
+// the extra registers cost more warps than the deeper loads gain).
+template <class P>
+struct Flat3L {
+  template <int R>
+  static int go(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, int steps) {
+    constexpr int kChunk = 32 * R * (16 / (int)sizeof(typename P::InT));
+    const int nch = steps / kChunk;
+    if (nch <= 4) return launch_flat3<P, 4, R>(p, g, ws, wsb, s);
+    if (nch <= 8) return launch_flat3<P, 8, R>(p, g, ws, wsb, s);
+    return launch_flat3<P, 16, R>(p, g, ws, wsb, s);
+  }
+  static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+    const int steps = env_int("RLS_FLAT3_STEPS", 2048);
+    return go<1>(p, g, ws, wsb, s, steps);
+  }
+};
+
+// flat2 tiles: R rounds of 32 lanes x one 16-byte vector (RLS_FLAT2_R = 1, 2, 4).
 template <class P>
 struct Flat2L {
-  static int run(const typename P::Params& p, const Geom& g0, void* ws, size_t wsb, cudaStream_t s) {
-    constexpr int R = sizeof(typename P::InT) == 4 ? 4 : 2;  // 512-element tiles
-    constexpr int64_t CH = 32LL * R * (16 / (int)sizeof(typename P::InT));
-    Geom g = g0;
-    g.num_tiles = (g.M + CH - 1) / CH;
-    if (g.num_tiles == 0) return RLS_OK;
-    if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
-    g.ws_cap = ws ? ws_capacity(wsb) : 0;
-    if (g.ws_cap < g.num_tiles) return RLS_EWORKSPACE;
-    // Same convention as the other look-back kernels: a launch uses the current
-    // epoch and leaves the next one for the following launch on this workspace.
-    flat2_kernel<P, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
-    advance_epoch<<<1, 1, 0, s>>>(ws);
-    return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+    const int r = env_int("RLS_FLAT2_R", 4);
+    if (r == 1) return launch_flat2<P, 1>(p, g, ws, wsb, s);
+    if (r == 2) return launch_flat2<P, 2>(p, g, ws, wsb, s);
+    return launch_flat2<P, 4>(p, g, ws, wsb, s);
   }
 };
 
@@ -327,9 +374,10 @@ int family(const Geom& g) {
   if (m == 3) return 3;
   if (m == 4) return rows_ok ? 4 : 0;
   if (m == 5) return rows_ok ? 5 : 3;
+  if (m == 6) return rows_ok ? 6 : 3;
   if (m != 0) return 0;
   if (rows_ok && g.N >= kRowsMinEnvs) return 4;
-  return rows_ok ? 5 : 3;
+  return rows_ok ? 6 : 3;
 }
 
 template <class Alg, int MAXR = 4>
@@ -373,7 +421,9 @@ extern "C" {
 size_t rls_workspace_bytes(int64_t num_elements) {
   if (num_elements <= 0) return 64;
   const int64_t tiles = (num_elements + kMinTileElems - 1) / kMinTileElems;
-  return ws_bytes_for_tiles(tiles);
+  const size_t packed = 64 + (size_t)tiles * 24;  // flat2's three 8-byte words per tile
+  const size_t flags = ws_bytes_for_tiles(tiles);
+  return packed > flags ? packed : flags;
 }
 
 int rls_workspace_error(void* ws, void* stream) {
@@ -447,6 +497,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       if (fam == 3) return gae_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return gae_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return gae_v<Flat2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return gae_v<Flat3L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -456,6 +507,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       if (fam == 3) return gae_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return gae_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return gae_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return gae_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -495,6 +547,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       if (fam == 3) return vtrace_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return vtrace_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return vtrace_v<Flat2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return vtrace_v<Flat3L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
@@ -504,6 +557,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       if (fam == 3) return vtrace_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return vtrace_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return vtrace_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return vtrace_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -534,7 +588,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   p.gamma = gamma; p.lam = lambda_; p.c_bar = c_bar; p.rho_bar = rho_bar;
   if (g.M == 0) return RLS_OK;
   const int mode = path_mode();
-  if (family<RetraceAlg>(g) == 3 || family<RetraceAlg>(g) == 5) {
+  if (family<RetraceAlg>(g) >= 5 || family<RetraceAlg>(g) == 3) {
     // Stage pi / Qn in the tile ring while a two-stage ring of them fits.
     const int64_t per_step = 8 * num_actions + 28;
     const bool staged = num_actions <= 16 && 2 * per_step * kTileThreads * 9 + 12 * kTileThreads * 9 <= 220 * 1024;
@@ -588,6 +642,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       if (fam == 3) return lambda_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return lambda_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return lambda_v<Flat2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return lambda_v<Flat3L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -597,6 +652,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       if (fam == 3) return lambda_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return lambda_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return lambda_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return lambda_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -630,6 +686,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       if (fam == 3) return discounted_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return discounted_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return discounted_v<Flat2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return discounted_v<Flat3L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -639,6 +696,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       if (fam == 3) return discounted_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return discounted_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return discounted_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return discounted_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -667,6 +725,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       if (fam == 3) return forward_v<TileL, float>(p, g, ws, ws_bytes, s);
       if (fam == 4) return forward_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return forward_v<Flat2L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return forward_v<Flat3L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -676,6 +735,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       if (fam == 3) return forward_v<TileL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 4) return forward_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return forward_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return forward_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -713,6 +773,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       if (fam == 3) return affine_v<TileL, true>(p, g, ws, ws_bytes, s);
       if (fam == 4) return affine_v<Rows2L, true>(p, g, ws, ws_bytes, s);
       if (fam == 5) return affine_v<Flat2L, true>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return affine_v<Flat3L, true>(p, g, ws, ws_bytes, s);
     }
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
@@ -722,6 +783,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       if (fam == 3) return affine_v<TileL, false>(p, g, ws, ws_bytes, s);
       if (fam == 4) return affine_v<Rows2L, false>(p, g, ws, ws_bytes, s);
       if (fam == 5) return affine_v<Flat2L, false>(p, g, ws, ws_bytes, s);
+      if (fam == 6) return affine_v<Flat3L, false>(p, g, ws, ws_bytes, s);
     }
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }
@@ -737,7 +799,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
 // consistent from call to call (epoch-tagged flags), and each call clears the
 // ticket / exit counters and the error latch before launching.
 namespace {
-constexpr int64_t kNoAllocTiles = RLS_NOALLOC_MAX_ELEMENTS / kMinTileElems;
+constexpr int64_t kNoAllocTiles = RLS_NOALLOC_MAX_ELEMENTS / 512;  // 512-step tiles (tile, flat kernels)
 constexpr size_t kNoAllocBytes = 64 + (size_t)kNoAllocTiles * 4 + (size_t)kNoAllocTiles * 16;
 static_assert(kNoAllocTiles * 4 % 16 == 0, "flag array keeps the aggregate array 16-byte aligned");
 

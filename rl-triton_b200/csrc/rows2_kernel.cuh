@@ -263,9 +263,8 @@ namespace rls {
 // flat2: one warp per 512-element tile of the flat [N*S] array, for few long
 // rows.  Each warp loads its tile straight into registers (the ChunkScan of the
 // row kernel), publishes the tile's map, takes its carry from a decoupled
-// look-back over the preceding tiles, and emits.  Tile t is scanned by warp
-// t % 4 of block t / 4 (blocks start in index order; every wait is bounded
-// anyway and latches an error bit instead of hanging).  A launch uses the
+// look-back over the preceding tiles, and emits (every wait is bounded and
+// latches an error bit instead of hanging).  A launch uses the
 // workspace's current epoch, like the other look-back kernels, and a one-thread
 // kernel launched right after it advances the epoch, so blocks need no exit
 // counter.
@@ -276,13 +275,46 @@ __global__ void advance_epoch(void* ws_base) {
   h->epoch = (h->epoch + 1u) & kEpochMask;
 }
 
+constexpr int kLookWindows = 4;
+
+// flat2's status words: per tile three 64-bit words, each carrying an fp32 value
+// in its low half and (epoch << 2 | kind) in its high half -- inc (the inclusive
+// value: kFlagIncl or kFlagSelf), aga / agb (the map's a and b: kFlagAgg).
+// A value and its tag travel in one aligned 64-bit store, so readers need no
+// fence and one round trip.  Layout: [64-byte header | inc | aga | agb].
+struct PackedWs {
+  WsHeader* hdr;
+  unsigned long long *inc, *aga, *agb;
+};
+__host__ __device__ inline int64_t packed_capacity(size_t bytes) {
+  return bytes < 64 ? 0 : (int64_t)((bytes - 64) / 24);
+}
+__device__ __forceinline__ PackedWs packed_carve(void* base, int64_t cap) {
+  PackedWs w;
+  w.hdr = reinterpret_cast<WsHeader*>(base);
+  w.inc = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(base) + 64);
+  w.aga = w.inc + cap;
+  w.agb = w.aga + cap;
+  return w;
+}
+__device__ __forceinline__ unsigned long long pack_word(float v, unsigned tk) {
+  return ((unsigned long long)tk << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ void st_word(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned word_tag(unsigned long long w) { return (unsigned)(w >> 32); }
+__device__ __forceinline__ float word_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
+
 // Carry entering tile `ticket` (the state after tile ticket-1), read from the
 // tiles published before it, 32 at a time (lane l reads tile ticket-1-32w-l).
-// A tile publishes its map (kFlagAgg), its exact inclusive value when the map
-// does not depend on the carry (kFlagSelf), and its inclusive value once its
-// own look-back is done (kFlagIncl).  The carry is the serial fold
-// c <- a_m + b_m * c from a stop point that depends only on the data, so the
-// outputs are bit-identical from run to run:
+// The carry is the serial fold c <- a_m + b_m * c from a stop point that
+// depends only on the data, so the outputs are bit-identical from run to run:
 //  * decaying recurrences: the nearest kFlagSelf tile, or the nearest tile where
 //    the running product of b's (taken from ticket-1 backwards) is exactly 0 --
 //    the fold starts from 0 there; for gamma*lambda decays this comes within a
@@ -292,8 +324,7 @@ __global__ void advance_epoch(void* ws_base) {
 //    the same result.
 // Without a stop within kLookWindows windows, the predecessor's own inclusive
 // value (computed by the same rule) is awaited instead.
-constexpr int kLookWindows = 4;
-__device__ __forceinline__ float flat2_look_back(const Workspace& ws, int64_t ticket, unsigned tag, int lane,
+__device__ __forceinline__ float flat2_look_back(const PackedWs& ws, int64_t ticket, unsigned tag, int lane,
                                                  bool unit, unsigned& err) {
   constexpr unsigned FULL = 0xffffffffu;
   float As[kLookWindows], Bs[kLookWindows];
@@ -307,22 +338,21 @@ __device__ __forceinline__ float flat2_look_back(const Workspace& ws, int64_t ti
     unsigned kind = kFlagSelf;
     float a = 0.f, b = 0.f, inc = 0.f;
     if (pj >= 0) {
-      unsigned f = 0, it = 0;
+      unsigned it = 0;
       while (true) {
-        f = ld_acquire_u32(&ws.flags[pj]);
-        if ((f & ~3u) == (tag & ~3u) && (f & 3u)) break;
-        if (++it > kSpinLimit) { err |= 1u; f = tag | kFlagSelf; break; }
+        const unsigned long long wi = ld_word(ws.inc + pj);
+        const unsigned ti = word_tag(wi);
+        if (ti == (tag | kFlagSelf)) { kind = kFlagSelf; inc = a = word_val(wi); break; }
+        const unsigned long long wa = ld_word(ws.aga + pj), wb = ld_word(ws.agb + pj);
+        if (word_tag(wa) == (tag | kFlagAgg) && word_tag(wb) == (tag | kFlagAgg)) {
+          a = word_val(wa);
+          b = word_val(wb);
+          kind = (ti == (tag | kFlagIncl)) ? kFlagIncl : kFlagAgg;
+          inc = word_val(wi);
+          break;
+        }
+        if (++it > kSpinLimit) { err |= 1u; kind = kFlagSelf; a = inc = 0.f; break; }
         if (it > 8) __nanosleep(32);
-      }
-      kind = f & 3u;
-      if (kind == kFlagSelf) {
-        inc = __ldcg(&ws.incl[pj]).x;
-        a = inc;
-      } else {
-        const float2 v = __ldcg(&ws.agg[pj]);
-        a = v.x;
-        b = v.y;
-        if (unit && kind == kFlagIncl) inc = __ldcg(&ws.incl[pj]).x;
       }
     }
     float pr = b;  // running product of b, nearest tile first
@@ -361,8 +391,9 @@ __device__ __forceinline__ float flat2_look_back(const Workspace& ws, int64_t ti
     if (lane == 0) {
       unsigned it = 0;
       while (true) {
-        const unsigned f = ld_acquire_u32(&ws.flags[ticket - 1]);
-        if ((f & ~3u) == (tag & ~3u) && (f & 3u) >= kFlagIncl) { v = __ldcg(&ws.incl[ticket - 1]).x; break; }
+        const unsigned long long wi = ld_word(ws.inc + ticket - 1);
+        const unsigned ti = word_tag(wi);
+        if (ti == (tag | kFlagIncl) || ti == (tag | kFlagSelf)) { v = word_val(wi); break; }
         if (++it > kSpinLimit) { err |= 1u; break; }
         __nanosleep(64);
       }
@@ -372,27 +403,18 @@ __device__ __forceinline__ float flat2_look_back(const Workspace& ws, int64_t ti
   return c;
 }
 
+// Scan, publish, look back and emit one loaded tile.
 template <class P, int R>
-__global__ void __launch_bounds__(128) flat2_kernel(const typename P::Params p, const Geom g, void* ws_base) {
+__device__ __forceinline__ void flat2_tile(const typename P::Params& p, const Geom& g, const PackedWs& ws,
+                                           int64_t ticket, int lane, unsigned tag, const Rows2Chunk<P, R>& ch,
+                                           unsigned& err) {
   using CS = ChunkScan<P, R>;
   constexpr int VEC = CS::VEC;
   constexpr int64_t CH = (int64_t)R * 32 * VEC;
   constexpr bool BWD = P::kBackward;
   constexpr unsigned FULL = 0xffffffffu;
-  __shared__ unsigned s_epoch;
-  const Workspace ws = ws_carve(ws_base, g.ws_cap);
-  if (threadIdx.x == 0) s_epoch = ld_relaxed_u32(&ws.hdr->epoch);
-  __syncthreads();
-  const unsigned tag = s_epoch << 2;
-  const int lane = threadIdx.x & 31;
-  const int64_t ticket = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (ticket >= g.num_tiles) return;
   const int64_t tile = BWD ? (g.num_tiles - 1 - ticket) : ticket;
   const int64_t base = tile * CH;
-  unsigned err = 0;
-
-  Rows2Chunk<P, R> ch;
-  rows2_load<P, R>(p, 0, g.M, base, lane, ch);
   CS cs;
 #pragma unroll
   for (int r = 0; r < R; ++r) {
@@ -410,11 +432,10 @@ __global__ void __launch_bounds__(128) flat2_kernel(const typename P::Params p, 
   const Pair agg = cs.aggregate();
   if (lane == 0) {
     if (agg.b == 0.f || ticket == 0) {
-      __stcg(&ws.incl[ticket], make_float2(agg.a, 0.f));
-      st_release_u32(&ws.flags[ticket], tag | kFlagSelf);
+      st_word(ws.inc + ticket, pack_word(agg.a, tag | kFlagSelf));
     } else {
-      __stcg(&ws.agg[ticket], make_float2(agg.a, agg.b));
-      st_release_u32(&ws.flags[ticket], tag | kFlagAgg);
+      st_word(ws.aga + ticket, pack_word(agg.a, tag | kFlagAgg));
+      st_word(ws.agb + ticket, pack_word(agg.b, tag | kFlagAgg));
     }
   }
   // The tile's entry element: backward the last lane's last element of the last round.
@@ -424,12 +445,166 @@ __global__ void __launch_bounds__(128) flat2_kernel(const typename P::Params p, 
   float carry = 0.f;
   if (need) {
     carry = flat2_look_back(ws, ticket, tag, lane, P::unit_decay(p), err);
-    if (lane == 0 && agg.b != 0.f) {
-      __stcg(&ws.incl[ticket], make_float2(apply(agg, carry), 0.f));
-      st_release_u32(&ws.flags[ticket], tag | kFlagIncl);
-    }
+    if (lane == 0 && agg.b != 0.f) st_word(ws.inc + ticket, pack_word(apply(agg, carry), tag | kFlagIncl));
   }
   cs.pass2(p, g, ch, carry);
+}
+
+template <class P, int R>
+__device__ __forceinline__ int64_t flat2_base(const Geom& g, int64_t ticket) {
+  constexpr int64_t CH = (int64_t)R * 32 * Rows2Chunk<P, R>::VEC;
+  return (P::kBackward ? (g.num_tiles - 1 - ticket) : ticket) * CH;
+}
+
+// One tile per warp: tile t is scanned by warp t % 4 of block t / 4.  Blocks
+// start in index order, so a tile's predecessors are running or done (the waits
+// are bounded regardless); dynamic block scheduling keeps slow warps from
+// holding up a fixed chain of successors.
+template <class P, int R>
+__global__ void __launch_bounds__(128) flat2_kernel(const typename P::Params p, const Geom g, void* ws_base) {
+  __shared__ unsigned s_epoch;
+  const PackedWs ws = packed_carve(ws_base, g.ws_cap);
+  if (threadIdx.x == 0) s_epoch = ld_relaxed_u32(&ws.hdr->epoch);
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= g.num_tiles) return;
+  unsigned err = 0;
+  Rows2Chunk<P, R> ch;
+  rows2_load<P, R>(p, 0, g.M, flat2_base<P, R>(g, t), lane, ch);
+  flat2_tile<P, R>(p, g, ws, t, lane, s_epoch << 2, ch, err);
+  if (err && lane == 0) atomicOr(&ws.hdr->error, err);
+}
+
+// ===========================================================================
+// flat3: one warp per super-tile of NCH chunks of R vectors per lane, walked twice.
+// Walk A streams the chunks from the carry-entry end (the next chunk's vectors
+// requested before the current one is scanned) and only composes the
+// super-tile's map; the map is published and the carry taken from the same
+// look-back as flat2; walk B re-reads the chunks -- from L2, where walk A left
+// them: the resident super-tiles hold ~50 MB -- and emits.  The look-back thus
+// sits between two long stretches of independent loads instead of inside every
+// small tile.
+// ===========================================================================
+template <class P, int R, bool LAST_USE>
+__device__ __forceinline__ void flat_load(const typename P::Params& p, int64_t M, int64_t cbase, int lane,
+                                          Rows2Chunk<P, R>& ch) {
+  constexpr int VEC = Rows2Chunk<P, R>::VEC;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int64_t i = cbase + (int64_t)r * 32 * VEC + lane * VEC;
+#pragma unroll
+    for (int k = 0; k < P::kNS; ++k) {
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const typename P::InT*>(P::sptr(p, k)) + i);
+      ch.v[r][k] = (i < M) ? (LAST_USE ? __ldcs(src) : __ldg(src)) : make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <class P, int R>
+__device__ __forceinline__ void flat_chunk_setup(const Geom& g, int64_t cbase, int lane, ChunkScan<P, R>& cs) {
+  constexpr int VEC = ChunkScan<P, R>::VEC;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    cs.i0[r] = cbase + (int64_t)r * 32 * VEC + lane * VEC;
+    cs.valid[r] = cs.i0[r] < g.M;
+    row_col(cs.i0[r], g.S, cs.row[r], cs.col0[r]);
+    cs.edge_v[r] = cs.valid[r] && (P::kBackward ? (cs.col0[r] + VEC == g.S) : (cs.col0[r] == 0));
+  }
+}
+
+template <class P, int NCH, int R>
+__global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, const Geom g, void* ws_base) {
+  using CS = ChunkScan<P, R>;
+  constexpr int RE = P::kBackward ? R - 1 : 0;  // round holding the entry element
+  constexpr int VEC = CS::VEC;
+  constexpr int64_t CH = 32 * VEC * R;
+  constexpr int64_t ST = CH * NCH;
+  constexpr bool BWD = P::kBackward;
+  constexpr unsigned FULL = 0xffffffffu;
+  __shared__ unsigned s_epoch;
+  const PackedWs ws = packed_carve(ws_base, g.ws_cap);
+  if (threadIdx.x == 0) s_epoch = ld_relaxed_u32(&ws.hdr->epoch);
+  __syncthreads();
+  const unsigned tag = s_epoch << 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t ticket = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (ticket >= g.num_tiles) return;
+  const int64_t base = (BWD ? (g.num_tiles - 1 - ticket) : ticket) * ST;
+  auto cbase = [&](int k) { return base + (BWD ? (NCH - 1 - k) : k) * CH; };
+  unsigned err = 0;
+  using Nbr = typename P::Nbr;
+  Nbr nb0{};
+  if constexpr (P::kNeedsNbr) {
+    const int64_t gn = BWD ? base + ST : base - 1;
+    if (BWD ? (gn < g.M) : (gn >= 0)) nb0 = P::nbr_global(p, gn);
+  }
+
+  // ---- walk A: the super-tile's map --------------------------------------------
+  Rows2Chunk<P, R> a, b;
+  Pair M = pair_identity();
+  bool keep = false;  // the entry element does not cut the carry
+  {
+    Nbr nb = nb0;
+    flat_load<P, R, false>(p, g.M, cbase(0), lane, a);
+#pragma unroll 1
+    for (int k = 0; k < NCH; k += 2) {
+      if (k + 1 < NCH) flat_load<P, R, false>(p, g.M, cbase(k + 1), lane, b);
+      {
+        CS cs;
+        flat_chunk_setup<P, R>(g, cbase(k), lane, cs);
+        nb = cs.pass1(p, g, lane, a, nb);
+        M = compose(cs.aggregate(), M);
+        if (k == 0) keep = P::kNextInEmit ? !cs.edge_v[RE] : (cs.cb[RE][CS::JE] != 0.f);
+      }
+      if (k + 1 >= NCH) break;
+      if (k + 2 < NCH) flat_load<P, R, false>(p, g.M, cbase(k + 2), lane, a);
+      {
+        CS cs;
+        flat_chunk_setup<P, R>(g, cbase(k + 1), lane, cs);
+        nb = cs.pass1(p, g, lane, b, nb);
+        M = compose(cs.aggregate(), M);
+      }
+    }
+  }
+  if (lane == 0) {
+    if (M.b == 0.f || ticket == 0) {
+      st_word(ws.inc + ticket, pack_word(M.a, tag | kFlagSelf));
+    } else {
+      st_word(ws.aga + ticket, pack_word(M.a, tag | kFlagAgg));
+      st_word(ws.agb + ticket, pack_word(M.b, tag | kFlagAgg));
+    }
+  }
+  const bool need = ticket > 0 && __shfl_sync(FULL, keep ? 1 : 0, BWD ? 31 : 0);
+  float carry = 0.f;
+  if (need) {
+    carry = flat2_look_back(ws, ticket, tag, lane, P::unit_decay(p), err);
+    if (lane == 0 && M.b != 0.f) st_word(ws.inc + ticket, pack_word(apply(M, carry), tag | kFlagIncl));
+  }
+
+  // ---- walk B: re-read (from L2) and emit ---------------------------------------
+  {
+    Nbr nb = nb0;
+    flat_load<P, R, true>(p, g.M, cbase(0), lane, a);
+#pragma unroll 1
+    for (int k = 0; k < NCH; k += 2) {
+      if (k + 1 < NCH) flat_load<P, R, true>(p, g.M, cbase(k + 1), lane, b);
+      {
+        CS cs;
+        flat_chunk_setup<P, R>(g, cbase(k), lane, cs);
+        nb = cs.pass1(p, g, lane, a, nb);
+        carry = cs.pass2(p, g, a, carry);
+      }
+      if (k + 1 >= NCH) break;
+      if (k + 2 < NCH) flat_load<P, R, true>(p, g.M, cbase(k + 2), lane, a);
+      {
+        CS cs;
+        flat_chunk_setup<P, R>(g, cbase(k + 1), lane, cs);
+        nb = cs.pass1(p, g, lane, b, nb);
+        carry = cs.pass2(p, g, b, carry);
+      }
+    }
+  }
   if (err && lane == 0) atomicOr(&ws.hdr->error, err);
 }
 

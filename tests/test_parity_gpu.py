@@ -33,7 +33,7 @@ def T(a, dev="cuda", dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)
 
 
-@pytest.fixture(autouse=True, params=["auto", "rows2", "flat2", "tile", "rows", "flat"])
+@pytest.fixture(autouse=True, params=["auto", "rows2", "flat3", "flat2", "tile", "rows", "flat"])
 def kernel_path(request, monkeypatch):
     """Run every case on each kernel family: the library's own choice ("auto"),
     the TMA-staged tile kernel, the row-parallel register kernel (one warp per
@@ -323,7 +323,7 @@ def test_kernel_families_share_one_workspace():
     from rl_triton import _native as nat
     old = os.environ.get("RLS_PATH")
     try:
-        for path in ["flat2", "tile", "flat", "flat2", "flat", "tile", "flat2"]:
+        for path in ["flat3", "flat2", "tile", "flat3", "flat", "flat2", "flat3", "tile", "flat2"]:
             os.environ["RLS_PATH"] = path
             for n, t in [(64, 512), (1, 4095), (3, 5000)]:
                 x = rng_inputs(n, t, seed=n + t)
