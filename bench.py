@@ -552,6 +552,8 @@ def run_ncu(args, local):
     cfg = CONFIGS[args.config]
     if args.envs:
         cfg = dict(cfg, N=args.envs)
+    if args.len:
+        cfg = dict(cfg, T=args.len)
     dev = torch.device("cuda", local)
     x = make_inputs(cfg, dev, seed=1)
     calls = make_calls(cfg, x)
@@ -594,6 +596,7 @@ def main():
                          "function, in --config order; no timing, no graphs, prints nothing")
     ap.add_argument("--only", default="", help="comma list of functions to run (default: all of the config)")
     ap.add_argument("--envs", type=int, default=0, help="--ncu mode: override num_envs (a smaller slice to profile)")
+    ap.add_argument("--len", type=int, default=0, help="--ncu mode: override the sequence length T")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

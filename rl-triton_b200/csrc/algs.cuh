@@ -40,6 +40,7 @@ struct Geom {
   int seg;            // 1: time-split launch (halo neighbours at cuts)
   int smem_per_warp;  // dynamic shared memory per warp (Retrace staging)
   int tma;            // 1: staging uses cp.async.bulk
+  int l2_prefetch;    // flat3: bulk L2 prefetch of each super-tile before its first walk
 };
 
 // Struct-generic warp shuffles for neighbour records (all 32-bit members).

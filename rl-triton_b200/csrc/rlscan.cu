@@ -129,6 +129,7 @@ int path_mode() {
   if (!std::strcmp(s, "rows2")) return 4;
   if (!std::strcmp(s, "flat2")) return 5;
   if (!std::strcmp(s, "flat3")) return 6;
+  if (!std::strcmp(s, "flat4")) return 7;
   return 0;
 }
 
@@ -285,6 +286,7 @@ int launch_flat3(const typename P::Params& p, const Geom& g0, void* ws, size_t w
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   g.ws_cap = ws ? packed_capacity(wsb) : 0;
   if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
+  g.l2_prefetch = env_int("RLS_FLAT3_PF", 0);
   flat3_kernel<P, NCH, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
   advance_epoch<<<1, 1, 0, s>>>(ws);
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
@@ -306,6 +308,67 @@ struct Flat3L {
   static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
     const int steps = env_int("RLS_FLAT3_STEPS", 2048);
     return go<1>(p, g, ws, wsb, s, steps);
+  }
+};
+
+template <class P, int NCH, int D, int G>
+int launch_flat4(const typename P::Params& p, const Geom& g0, void* ws, size_t wsb, cudaStream_t s) {
+  constexpr int64_t ST = 32LL * NCH * G * (16 / (int)sizeof(typename P::InT));
+  constexpr int kWarp = flat4_smem_per_warp<P, D, G, NCH>();
+  if constexpr (kWarp > 200 * 1024) {
+    return launch_flat4<P, NCH, 4, G>(p, g0, ws, wsb, s);  // a resident super-tile this large does not fit
+  } else {
+  constexpr int WPB = 4 * kWarp <= 200 * 1024 ? 4 : (2 * kWarp <= 200 * 1024 ? 2 : 1);
+  constexpr int kSmem = WPB * kWarp;
+  static_assert(kSmem <= 200 * 1024, "ring too large");
+  Geom g = g0;
+  g.num_tiles = (g.M + ST - 1) / ST;
+  if (g.num_tiles == 0) return RLS_OK;
+  if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
+  g.ws_cap = ws ? packed_capacity(wsb) : 0;
+  if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
+  g.l2_prefetch = 0;
+  static bool attr = false;  // per instantiation; racing first calls set the same value
+  if (!attr) {
+    if (cudaFuncSetAttribute(flat4_kernel<P, NCH, D, G, WPB>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) !=
+        cudaSuccess)
+      return RLS_ECUDA;
+    attr = true;
+  }
+  flat4_kernel<P, NCH, D, G, WPB><<<(unsigned)((g.num_tiles + WPB - 1) / WPB), WPB * 32, kSmem, s>>>(p, g, ws);
+  advance_epoch<<<1, 1, 0, s>>>(ws);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  }
+}
+
+// flat4: RLS_FLAT3_STEPS per super-tile as flat3; RLS_FLAT4_D ring slots (3 or
+// 4); RLS_FLAT4_EPL steps per lane and chunk (8 or 16; rows must be a multiple).
+template <class P>
+struct Flat4L {
+  static constexpr int V0 = 16 / (int)sizeof(typename P::InT);
+  template <int D, int G>
+  static int go(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, int steps) {
+    constexpr int kChunk = 32 * V0 * G;
+    const int nch = steps / kChunk;
+    if (nch <= 4) return launch_flat4<P, 4, D, G>(p, g, ws, wsb, s);
+    if (nch <= 8) return launch_flat4<P, 8, D, G>(p, g, ws, wsb, s);
+    return launch_flat4<P, 16, D, G>(p, g, ws, wsb, s);
+  }
+  template <int G>
+  static int d(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, int steps) {
+    const int dd = env_int("RLS_FLAT4_D", 4);
+    if (dd == 0) return go<0, G>(p, g, ws, wsb, s, steps);
+    return dd == 3 ? go<3, G>(p, g, ws, wsb, s, steps) : go<4, G>(p, g, ws, wsb, s, steps);
+  }
+  static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+    const int steps = env_int("RLS_FLAT3_STEPS", 2048);
+    const int epl = env_int("RLS_FLAT4_EPL", 16);
+    int gsel = epl / V0;
+    if (gsel > 4) gsel = 4;
+    while (gsel > 1 && g.S % (V0 * gsel) != 0) gsel /= 2;
+    if (gsel >= 4) return d<4>(p, g, ws, wsb, s, steps);
+    if (gsel == 2) return d<2>(p, g, ws, wsb, s, steps);
+    return d<1>(p, g, ws, wsb, s, steps);
   }
 };
 
@@ -375,6 +438,7 @@ int family(const Geom& g) {
   if (m == 4) return rows_ok ? 4 : 0;
   if (m == 5) return rows_ok ? 5 : 3;
   if (m == 6) return rows_ok ? 6 : 3;
+  if (m == 7) return rows_ok ? 7 : 3;
   if (m != 0) return 0;
   if (rows_ok && g.N >= kRowsMinEnvs) return 4;
   return rows_ok ? 6 : 3;
@@ -498,6 +562,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       if (fam == 4) return gae_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return gae_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return gae_v<Flat3L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return gae_v<Flat4L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -508,6 +573,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       if (fam == 4) return gae_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return gae_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return gae_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return gae_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -548,6 +614,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       if (fam == 4) return vtrace_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return vtrace_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return vtrace_v<Flat3L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return vtrace_v<Flat4L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
@@ -558,6 +625,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       if (fam == 4) return vtrace_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return vtrace_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return vtrace_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return vtrace_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -643,6 +711,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       if (fam == 4) return lambda_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return lambda_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return lambda_v<Flat3L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return lambda_v<Flat4L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -653,6 +722,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       if (fam == 4) return lambda_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return lambda_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return lambda_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return lambda_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -687,6 +757,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       if (fam == 4) return discounted_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return discounted_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return discounted_v<Flat3L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return discounted_v<Flat4L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -697,6 +768,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       if (fam == 4) return discounted_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return discounted_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return discounted_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return discounted_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -726,6 +798,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       if (fam == 4) return forward_v<Rows2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 5) return forward_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return forward_v<Flat3L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return forward_v<Flat4L, float>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -736,6 +809,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       if (fam == 4) return forward_v<Rows2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 5) return forward_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return forward_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return forward_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -774,6 +848,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       if (fam == 4) return affine_v<Rows2L, true>(p, g, ws, ws_bytes, s);
       if (fam == 5) return affine_v<Flat2L, true>(p, g, ws, ws_bytes, s);
       if (fam == 6) return affine_v<Flat3L, true>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return affine_v<Flat4L, true>(p, g, ws, ws_bytes, s);
     }
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
@@ -784,6 +859,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       if (fam == 4) return affine_v<Rows2L, false>(p, g, ws, ws_bytes, s);
       if (fam == 5) return affine_v<Flat2L, false>(p, g, ws, ws_bytes, s);
       if (fam == 6) return affine_v<Flat3L, false>(p, g, ws, ws_bytes, s);
+      if (fam == 7) return affine_v<Flat4L, false>(p, g, ws, ws_bytes, s);
     }
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }

@@ -18,10 +18,13 @@
 
 namespace rls {
 
-template <class P, int R>
+// G: 16-byte vectors per lane and round, contiguous in memory (a lane owns
+// VEC = G * 16 / sizeof(InT) consecutive steps); stream k's vector g is v[r][k * G + g].
+template <class P, int R, int G = 1>
 struct Rows2Chunk {
-  static constexpr int VEC = 16 / (int)sizeof(typename P::InT);
-  uint4 v[R][P::kNS];
+  static constexpr int V0 = 16 / (int)sizeof(typename P::InT);
+  static constexpr int VEC = V0 * G;
+  uint4 v[R][P::kNS * G];
 };
 
 template <class P, int R>
@@ -39,22 +42,26 @@ __device__ __forceinline__ void rows2_load(const typename P::Params& p, int64_t 
   }
 }
 
-template <class P, int R>
-__device__ __forceinline__ void rows2_unpack(const Rows2Chunk<P, R>& ch, int r,
-                                             float (&in)[P::kNI][Rows2Chunk<P, R>::VEC], unsigned mask = ~0u) {
+template <class P, int R, int G = 1>
+__device__ __forceinline__ void rows2_unpack(const Rows2Chunk<P, R, G>& ch, int r,
+                                             float (&in)[P::kNI][Rows2Chunk<P, R, G>::VEC], unsigned mask = ~0u) {
+  constexpr int V0 = Rows2Chunk<P, R, G>::V0;
 #pragma unroll
   for (int k = 0; k < P::kNS; ++k) {
     if (!((mask >> k) & 1u)) continue;
-    const uint4 v = ch.v[r][k];
-    if constexpr (sizeof(typename P::InT) == 4) {
-      in[k][0] = __uint_as_float(v.x); in[k][1] = __uint_as_float(v.y);
-      in[k][2] = __uint_as_float(v.z); in[k][3] = __uint_as_float(v.w);
-    } else {
-      const unsigned w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        in[k][2 * h] = __uint_as_float(w[h] << 16);
-        in[k][2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+    for (int gg = 0; gg < G; ++gg) {
+      const uint4 v = ch.v[r][k * G + gg];
+      if constexpr (sizeof(typename P::InT) == 4) {
+        in[k][gg * V0 + 0] = __uint_as_float(v.x); in[k][gg * V0 + 1] = __uint_as_float(v.y);
+        in[k][gg * V0 + 2] = __uint_as_float(v.z); in[k][gg * V0 + 3] = __uint_as_float(v.w);
+      } else {
+        const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          in[k][gg * V0 + 2 * h] = __uint_as_float(w[h] << 16);
+          in[k][gg * V0 + 2 * h + 1] = __uint_as_float(w[h] & 0xffff0000u);
+        }
       }
     }
   }
@@ -63,10 +70,11 @@ __device__ __forceinline__ void rows2_unpack(const Rows2Chunk<P, R>& ch, int r,
 // One chunk (R rounds x 32 lanes x VEC elements) in registers: pass 1 builds
 // the element maps and the shuffle scans, pass 2 emits from the carry.  Lane
 // l's vector of round r starts at flat index i0[r] = (row, col0[r]).
-template <class P, int R>
+template <class P, int R, int G = 1>
 struct ChunkScan {
   using Nbr = typename P::Nbr;
-  static constexpr int VEC = Rows2Chunk<P, R>::VEC;
+  using Chunk = Rows2Chunk<P, R, G>;
+  static constexpr int VEC = Chunk::VEC;
   static constexpr int NI = P::kNI;
   static constexpr bool BWD = P::kBackward;
   static constexpr int JE = BWD ? VEC - 1 : 0;
@@ -79,15 +87,18 @@ struct ChunkScan {
   // edge_nbr: the neighbour across the chunk's carry-entry edge (element after
   // the chunk backward, before it forward); returns the one the next chunk in
   // walk order needs from this chunk.
+  // AGG_ONLY: only the chunk's total map is wanted (tot[]; excl[] is left
+  // unset) -- one butterfly reduction instead of the scan.
+  template <bool AGG_ONLY = false>
   __device__ __forceinline__ Nbr pass1(const typename P::Params& p, const Geom& g, int lane,
-                                       const Rows2Chunk<P, R>& ch, Nbr edge_nbr) {
+                                       const Chunk& ch, Nbr edge_nbr) {
     const int glob = g.edge_global;
     if constexpr (P::kNeedsNbr) {
       Nbr own[R];
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         float in[NI][VEC];
-        rows2_unpack<P, R>(ch, r, in);
+        rows2_unpack<P, R, G>(ch, r, in);
         own[r] = P::template nbr_of<VEC>(in, BWD ? 0 : VEC - 1);
       }
 #pragma unroll
@@ -109,7 +120,7 @@ struct ChunkScan {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       float in[NI][VEC];
-      rows2_unpack<P, R>(ch, r, in);
+      rows2_unpack<P, R, G>(ch, r, in);
       const EdgeLoc L{i0[r], row[r], col0[r], g.S, glob};
       Nbr nb{};
       if constexpr (P::kNeedsNbr) nb = nbe[r];
@@ -128,6 +139,17 @@ struct ChunkScan {
       for (int q = 0; q < VEC; ++q) {
         const int e = BWD ? (VEC - 1 - q) : q;
         m = compose(Pair{ca[r][e], cb[r][e]}, m);
+      }
+      if constexpr (AGG_ONLY) {
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const Pair o{__shfl_xor_sync(0xffffffffu, m.a, d), __shfl_xor_sync(0xffffffffu, m.b, d)};
+          // the lane half that comes later in walk order composes on the outside
+          const bool later = BWD ? !(lane & d) : (lane & d);
+          m = later ? compose(m, o) : compose(o, m);
+        }
+        tot[r] = m;
+        continue;
       }
       Pair incl = m;
 #pragma unroll
@@ -167,7 +189,7 @@ struct ChunkScan {
   }
 
   // Emit and store with the carry entering the chunk; returns the carry leaving it.
-  __device__ __forceinline__ float pass2(const typename P::Params& p, const Geom& g, const Rows2Chunk<P, R>& ch,
+  __device__ __forceinline__ float pass2(const typename P::Params& p, const Geom& g, const Chunk& ch,
                                          float carry) {
     const int glob = g.edge_global;
     float cr[R];
@@ -182,7 +204,7 @@ struct ChunkScan {
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       float in[NI][VEC];
-      if constexpr (P::kEmitReads) rows2_unpack<P, R>(ch, r, in, P::kEmitMask);
+      if constexpr (P::kEmitReads) rows2_unpack<P, R, G>(ch, r, in, P::kEmitMask);
       const EdgeLoc L{i0[r], row[r], col0[r], g.S, glob};
       float x = apply(excl[r], cr[r]);
       float o0[VEC], o1[VEC];
@@ -501,15 +523,41 @@ __device__ __forceinline__ void flat_load(const typename P::Params& p, int64_t M
   }
 }
 
-template <class P, int R>
-__device__ __forceinline__ void flat_chunk_setup(const Geom& g, int64_t cbase, int lane, ChunkScan<P, R>& cs) {
-  constexpr int VEC = ChunkScan<P, R>::VEC;
+// Row and column of a lane's vector.  Within one walk the chunks are CH steps
+// apart, so for rows of at least CH steps the position advances with one
+// compare (at most one row boundary is crossed) instead of a division per chunk.
+struct RowCursor {
+  int64_t row, col;
+};
+
+template <class P, int R, int G = 1>
+__device__ __forceinline__ void flat_chunk_setup(const Geom& g, int64_t cbase, int lane, bool first, RowCursor& c,
+                                                 ChunkScan<P, R, G>& cs) {
+  constexpr int VEC = ChunkScan<P, R, G>::VEC;
+  constexpr int64_t CH = 32 * VEC * R;
+  if constexpr (R == 1) {
+    cs.i0[0] = cbase + lane * VEC;
+    if (first || g.S < CH) {
+      row_col(cs.i0[0], g.S, c.row, c.col);
+    } else if (P::kBackward) {
+      c.col -= CH;
+      if (c.col < 0) { c.col += g.S; --c.row; }
+    } else {
+      c.col += CH;
+      if (c.col >= g.S) { c.col -= g.S; ++c.row; }
+    }
+    cs.row[0] = c.row;
+    cs.col0[0] = c.col;
+    cs.valid[0] = cs.i0[0] < g.M;
+    cs.edge_v[0] = cs.valid[0] && (P::kBackward ? (c.col + VEC == g.S) : (c.col == 0));
+  } else {
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    cs.i0[r] = cbase + (int64_t)r * 32 * VEC + lane * VEC;
-    cs.valid[r] = cs.i0[r] < g.M;
-    row_col(cs.i0[r], g.S, cs.row[r], cs.col0[r]);
-    cs.edge_v[r] = cs.valid[r] && (P::kBackward ? (cs.col0[r] + VEC == g.S) : (cs.col0[r] == 0));
+    for (int r = 0; r < R; ++r) {
+      cs.i0[r] = cbase + (int64_t)r * 32 * VEC + lane * VEC;
+      cs.valid[r] = cs.i0[r] < g.M;
+      row_col(cs.i0[r], g.S, cs.row[r], cs.col0[r]);
+      cs.edge_v[r] = cs.valid[r] && (P::kBackward ? (cs.col0[r] + VEC == g.S) : (cs.col0[r] == 0));
+    }
   }
 }
 
@@ -540,8 +588,19 @@ __global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, 
     if (BWD ? (gn < g.M) : (gn >= 0)) nb0 = P::nbr_global(p, gn);
   }
 
+  // One bulk L2 prefetch per input stream for the whole super-tile: walk A's
+  // loads then find their lines on the way, without registers held for them.
+  if (g.l2_prefetch) {
+    if (lane < P::kNS) {
+      const int64_t n = (g.M - base < ST ? g.M - base : ST);
+      const char* src = reinterpret_cast<const char*>(reinterpret_cast<const typename P::InT*>(P::sptr(p, lane)) + base);
+      const unsigned bytes = (unsigned)(n * (int64_t)sizeof(typename P::InT));
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+    }
+  }
   // ---- walk A: the super-tile's map --------------------------------------------
   Rows2Chunk<P, R> a, b;
+  RowCursor cur;
   Pair M = pair_identity();
   bool keep = false;  // the entry element does not cut the carry
   {
@@ -552,8 +611,8 @@ __global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, 
       if (k + 1 < NCH) flat_load<P, R, false>(p, g.M, cbase(k + 1), lane, b);
       {
         CS cs;
-        flat_chunk_setup<P, R>(g, cbase(k), lane, cs);
-        nb = cs.pass1(p, g, lane, a, nb);
+        flat_chunk_setup<P, R>(g, cbase(k), lane, k == 0, cur, cs);
+        nb = cs.template pass1<true>(p, g, lane, a, nb);
         M = compose(cs.aggregate(), M);
         if (k == 0) keep = P::kNextInEmit ? !cs.edge_v[RE] : (cs.cb[RE][CS::JE] != 0.f);
       }
@@ -561,8 +620,8 @@ __global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, 
       if (k + 2 < NCH) flat_load<P, R, false>(p, g.M, cbase(k + 2), lane, a);
       {
         CS cs;
-        flat_chunk_setup<P, R>(g, cbase(k + 1), lane, cs);
-        nb = cs.pass1(p, g, lane, b, nb);
+        flat_chunk_setup<P, R>(g, cbase(k + 1), lane, false, cur, cs);
+        nb = cs.template pass1<true>(p, g, lane, b, nb);
         M = compose(cs.aggregate(), M);
       }
     }
@@ -591,7 +650,7 @@ __global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, 
       if (k + 1 < NCH) flat_load<P, R, true>(p, g.M, cbase(k + 1), lane, b);
       {
         CS cs;
-        flat_chunk_setup<P, R>(g, cbase(k), lane, cs);
+        flat_chunk_setup<P, R>(g, cbase(k), lane, k == 0, cur, cs);
         nb = cs.pass1(p, g, lane, a, nb);
         carry = cs.pass2(p, g, a, carry);
       }
@@ -599,12 +658,195 @@ __global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, 
       if (k + 2 < NCH) flat_load<P, R, true>(p, g.M, cbase(k + 2), lane, a);
       {
         CS cs;
-        flat_chunk_setup<P, R>(g, cbase(k + 1), lane, cs);
+        flat_chunk_setup<P, R>(g, cbase(k + 1), lane, false, cur, cs);
         nb = cs.pass1(p, g, lane, b, nb);
         carry = cs.pass2(p, g, b, carry);
       }
     }
   }
+  if (err && lane == 0) atomicOr(&ws.hdr->error, err);
+}
+
+// ===========================================================================
+// flat4: flat3's two walks fed through a per-lane ring of D chunk slots in
+// shared memory, filled by 16-byte cp.async copies.  Each lane copies and later
+// reads back only its own vector of each stream, so the ring needs no barrier
+// and no cross-lane fence: cp.async.wait_group on the lane's own copies is the
+// whole protocol.  D-1 chunks per warp are in flight at all times, held in
+// shared memory rather than registers, and the loads of walk B's first chunks
+// are issued before the look-back, so they overlap it.
+// Ring layout per warp: [slot][stream][lane] x 16 bytes (a warp touches 512
+// contiguous bytes per stream: conflict-free).
+// ===========================================================================
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, unsigned src_bytes) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// D == 0: the ring holds the whole super-tile (NCH slots); walk B then re-reads
+// shared memory instead of L2.
+template <class P, int D, int G, int NCH = 0>
+constexpr int flat4_smem_per_warp() { return (D ? D : NCH) * P::kNS * 32 * G * 16; }
+
+// cp.async.wait_group takes an immediate: dispatch a run-time count (< 16).
+__device__ __forceinline__ void cp_async_wait_n(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    case 7: cp_async_wait<7>(); break;
+    case 8: cp_async_wait<8>(); break;
+    case 9: cp_async_wait<9>(); break;
+    case 10: cp_async_wait<10>(); break;
+    case 11: cp_async_wait<11>(); break;
+    case 12: cp_async_wait<12>(); break;
+    case 13: cp_async_wait<13>(); break;
+    case 14: cp_async_wait<14>(); break;
+    default: cp_async_wait<15>(); break;
+  }
+}
+
+// Position of 16-byte vector v (0 .. 32G-1, in memory order) inside its slot.
+// Copies are coalesced (lane l lands vectors g*32 + l), reads are per lane
+// (lane l takes vectors l*G .. l*G+G-1); the XOR keeps both conflict-free: any
+// 8 lanes of one phase hit 8 distinct 16-byte bank groups, for G = 2 and 4.
+template <int G>
+__device__ __forceinline__ int ring_pos(int v) {
+  if constexpr (G == 1) return v;
+  else return v ^ ((v >> (G == 2 ? 1 : 2)) & 7);
+}
+
+template <class P, int NCH, int D, int G, int WPB>
+__global__ void __launch_bounds__(WPB * 32) flat4_kernel(const typename P::Params p, const Geom g, void* ws_base) {
+  using CS = ChunkScan<P, 1, G>;
+  constexpr int NS = P::kNS;
+  constexpr int VEC = CS::VEC;
+  constexpr int V0 = CS::Chunk::V0;
+  static_assert(G == 1 || G == 2 || G == 4, "G");
+  constexpr int64_t CH = 32 * VEC;
+  constexpr int64_t ST = CH * NCH;
+  constexpr bool BWD = P::kBackward;
+  constexpr unsigned FULL = 0xffffffffu;
+  constexpr bool RES = D == 0;  // resident super-tile
+  constexpr int NSLOT = RES ? NCH : D;
+  static_assert(RES || D >= 2, "ring of at least two slots");
+  static_assert(!RES || NCH <= 16, "wait counts up to 15");
+  extern __shared__ uint4 flat4_ring[];
+  __shared__ unsigned s_epoch;
+  const PackedWs ws = packed_carve(ws_base, g.ws_cap);
+  if (threadIdx.x == 0) s_epoch = ld_relaxed_u32(&ws.hdr->epoch);
+  __syncthreads();
+  const unsigned tag = s_epoch << 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t ticket = (int64_t)blockIdx.x * WPB + (threadIdx.x >> 5);
+  if (ticket >= g.num_tiles) return;
+  uint4* ring = flat4_ring + (threadIdx.x >> 5) * (NSLOT * NS * 32 * G);
+  const int64_t base = (BWD ? (g.num_tiles - 1 - ticket) : ticket) * ST;
+  auto cbase = [&](int k) { return base + (BWD ? (NCH - 1 - k) : k) * CH; };
+
+  // Load j of the 2*NCH in walk order (walk A's chunks, then walk B's again)
+  // into slot j % D; one commit group per load, empty past the end, so that
+  // after load j + D - 1 is issued, wait_group<D-1> means "load j has landed".
+  auto issue = [&](int j) {
+    if (j < (RES ? NCH : 2 * NCH)) {
+      const int64_t cb = cbase(j < NCH ? j : j - NCH);
+      uint4* slot = ring + (j % NSLOT) * NS * 32 * G;
+#pragma unroll
+      for (int gg = 0; gg < G; ++gg) {
+        const int v = gg * 32 + lane;
+        const int64_t i = cb + (int64_t)v * V0;
+        const bool ok = i < g.M;
+        const int pos = ring_pos<G>(v);
+#pragma unroll
+        for (int k = 0; k < NS; ++k) {
+          const typename P::InT* src = reinterpret_cast<const typename P::InT*>(P::sptr(p, k));
+          cp_async16(slot + k * 32 * G + pos, ok ? src + i : src, ok ? 16u : 0u);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+  auto take = [&](int j, typename CS::Chunk& ch) {
+    if constexpr (RES) {
+      if (j < NCH) cp_async_wait_n(NCH - 1 - j);
+    } else {
+      cp_async_wait<D - 1>();
+    }
+    const uint4* slot = ring + (j % NSLOT) * NS * 32 * G;
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg) {
+      const int pos = ring_pos<G>(lane * G + gg);
+#pragma unroll
+      for (int k = 0; k < NS; ++k) ch.v[0][k * G + gg] = slot[k * 32 * G + pos];
+    }
+  };
+
+#pragma unroll
+  for (int j = 0; j < (RES ? NCH : D - 1); ++j) issue(j);
+
+  unsigned err = 0;
+  using Nbr = typename P::Nbr;
+  Nbr nb0{};
+  if constexpr (P::kNeedsNbr) {
+    const int64_t gn = BWD ? base + ST : base - 1;
+    if (BWD ? (gn < g.M) : (gn >= 0)) nb0 = P::nbr_global(p, gn);
+  }
+
+  // ---- walk A: the super-tile's map --------------------------------------------
+  typename CS::Chunk ch;
+  RowCursor cur;
+  Pair M = pair_identity();
+  bool keep = false;
+  {
+    Nbr nb = nb0;
+#pragma unroll 1
+    for (int k = 0; k < NCH; ++k) {
+      // slot (k + D - 1) % D was read into registers by the previous step
+      if constexpr (!RES) issue(k + D - 1);
+      take(k, ch);
+      CS cs;
+      flat_chunk_setup<P, 1, G>(g, cbase(k), lane, k == 0, cur, cs);
+      nb = cs.template pass1<true>(p, g, lane, ch, nb);
+      M = compose(cs.aggregate(), M);
+      if (k == 0) keep = P::kNextInEmit ? !cs.edge_v[0] : (cs.cb[0][CS::JE] != 0.f);
+    }
+  }
+  if (lane == 0) {
+    if (M.b == 0.f || ticket == 0) {
+      st_word(ws.inc + ticket, pack_word(M.a, tag | kFlagSelf));
+    } else {
+      st_word(ws.aga + ticket, pack_word(M.a, tag | kFlagAgg));
+      st_word(ws.agb + ticket, pack_word(M.b, tag | kFlagAgg));
+    }
+  }
+  const bool need = ticket > 0 && __shfl_sync(FULL, keep ? 1 : 0, BWD ? 31 : 0);
+  float carry = 0.f;
+  if (need) {
+    carry = flat2_look_back(ws, ticket, tag, lane, P::unit_decay(p), err);
+    if (lane == 0 && M.b != 0.f) st_word(ws.inc + ticket, pack_word(apply(M, carry), tag | kFlagIncl));
+  }
+
+  // ---- walk B: the same chunks again (L2) and emit ----------------------------------
+  {
+    Nbr nb = nb0;
+#pragma unroll 1
+    for (int k = 0; k < NCH; ++k) {
+      if constexpr (!RES) issue(NCH + k + D - 1);
+      take(NCH + k, ch);
+      CS cs;
+      flat_chunk_setup<P, 1, G>(g, cbase(k), lane, k == 0, cur, cs);
+      nb = cs.pass1(p, g, lane, ch, nb);
+      carry = cs.pass2(p, g, ch, carry);
+    }
+  }
+  cp_async_wait<0>();
   if (err && lane == 0) atomicOr(&ws.hdr->error, err);
 }
 
