@@ -7,6 +7,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "rlscan.h"
@@ -110,16 +111,19 @@ int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
 }
 
 // ---- kernel family ----------------------------------------------------------
-// RLS_PATH=auto (default) | rows2 | flat3 | flat2 | rows | flat | tile.  auto:
-// the lean row kernel (rows2) when every row starts 16-byte aligned and there
-// are enough rows to fill the GPU (one warp per row, no workspace, no barrier);
-// else, for aligned rows, flat3 (one warp per 2048-step super-tile walked twice
-// around one look-back, which also parallelises along time); else the
-// TMA-staged tile kernel.  flat2 is flat3's one-walk predecessor (one warp per
-// 512-step tile).  The others
-// force one family (the row kernels fall back to flat when rows are not
-// aligned); rows is the first row kernel with generic policies, kept as a
-// cross-check and for Retrace.
+// RLS_PATH=auto (default) | rows2 | vrows | flat4 | flat3 | flat2 | rows | flat |
+// tile.  auto: the lean row kernel (rows2) when every row starts 16-byte
+// aligned and there are enough rows to fill the GPU (one warp per row, no
+// workspace, no barrier); else, for aligned rows, virtual rows (vrows: the
+// flat buffer cut into ~32 segments per SM, one walk each with carry 0, then a
+// carry composition and a bounded fix-up) for scans whose output is the state
+// and whose segments reach 16K steps, and flat3 (one warp per 2048-step
+// super-tile walked twice around one look-back) for the rest; unaligned rows
+// take the TMA-staged tile kernel.  flat4 feeds flat3's walks through a
+// cp.async ring; flat2 is their one-walk predecessor (one warp per 512-step
+// tile).  The others force one family (the row kernels fall back to flat when
+// rows are not aligned); rows is the first row kernel with generic policies,
+// kept as a cross-check and for Retrace.
 int path_mode() {
   const char* s = std::getenv("RLS_PATH");
   if (!s || !*s) return 0;
@@ -130,6 +134,7 @@ int path_mode() {
   if (!std::strcmp(s, "flat2")) return 5;
   if (!std::strcmp(s, "flat3")) return 6;
   if (!std::strcmp(s, "flat4")) return 7;
+  if (!std::strcmp(s, "vrows")) return 8;
   return 0;
 }
 
@@ -372,6 +377,110 @@ struct Flat4L {
   }
 };
 
+}  // namespace
+
+namespace rls {
+// segment.cu: carry composition and bounded fix-up of the virtual rows.
+int vrows_finish(int alg, const void* f0, const void* f1, int bf16, float* out, int64_t M, int64_t S, float coef,
+                 int ends_at, float* seg_a, float* seg_b, float* carry, int* seg_code, int64_t nseg, int64_t L,
+                 cudaStream_t s);
+}  // namespace rls
+
+namespace {
+
+// ---- virtual rows -------------------------------------------------------------
+// Scans whose output is the state itself (GAE, lambda and discounted returns,
+// eligibility traces, prefix sums) on few long rows: cut the flat buffer into
+// ~32 segments per SM, scan each with carry 0 in one walk (vseg_kernel: no
+// second pass, no look-back), then compose the carries and apply the bounded
+// fix-up out[t] += P[t] * carry (vrows_finish), which touches each segment
+// only up to its first reset (or until P underflows).  Auto picks it when the
+// segments reach 16K steps and four times the decay's underflow length.
+struct VrowsSpec {
+  int alg;
+  const void* f0;
+  const void* f1;
+  float coef;
+  int ends_at;
+};
+template <class P>
+struct VSpec {
+  static constexpr bool ok = false;
+  static VrowsSpec get(const typename P::Params&) { return {}; }
+};
+template <class T, bool TR, int PB>
+struct VSpec<GaeT<T, TR, PB>> {
+  static constexpr bool ok = true;
+  static VrowsSpec get(const typename GaeT<T, TR, PB>::Params& p) { return {RLS_ALG_GAE, p.term, p.trunc, p.gl, 0}; }
+};
+template <class T, bool TR, bool PB>
+struct VSpec<LambdaT<T, TR, PB>> {
+  static constexpr bool ok = true;
+  static VrowsSpec get(const typename LambdaT<T, TR, PB>::Params& p) {
+    return {RLS_ALG_LAMBDA, p.term, p.trunc, p.gl, 0};
+  }
+};
+template <class T, bool TR, bool PB>
+struct VSpec<DiscountedT<T, TR, PB>> {
+  static constexpr bool ok = true;
+  static VrowsSpec get(const typename DiscountedT<T, TR, PB>::Params& p) {
+    return {RLS_ALG_DISCOUNTED, p.term, p.trunc, p.gamma, 0};
+  }
+};
+template <class T, bool PREV>
+struct VSpec<ForwardT<T, PREV>> {
+  static constexpr bool ok = true;
+  static VrowsSpec get(const typename ForwardT<T, PREV>::Params& p) {
+    // traces gate on done[t-1] with k = gamma*lambda; the prefix sum has k = 1
+    if (PREV && p.k != 1.f) return {RLS_ALG_ELIGIBILITY, p.done, nullptr, p.k, 1};
+    return {RLS_ALG_PREFIX, p.done, nullptr, 1.f, PREV ? 1 : 0};
+  }
+};
+
+constexpr int64_t kVrowsSegs = 32 * 148;  // segments: 32 warps per SM
+constexpr int64_t kVrowsMinLen = 16384;   // auto: shortest segment worth its fix-up
+
+// forced (RLS_PATH=vrows): any length; auto: only when segments reach
+// kVrowsMinLen.  Policies with other outputs fall back to flat3.
+template <class P>
+int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, bool forced) {
+  constexpr int64_t CH = 32 * (16 / (int)sizeof(typename P::InT));
+  if constexpr (!VSpec<P>::ok) {
+    return Flat3L<P>::run(p, g, ws, wsb, s);
+  } else {
+    if (g.M == 0) return RLS_OK;
+    // segments: kVrowsSegs, or as many as the workspace holds (four words each)
+    const int64_t room = ws && wsb > 64 ? (int64_t)((wsb - 64) / 16) : 0;
+    const int64_t want = room < kVrowsSegs ? room : kVrowsSegs;
+    if (want < 1) return Flat3L<P>::run(p, g, ws, wsb, s);
+    int64_t L = (g.M + want - 1) / want;
+    L = (L + CH - 1) / CH * CH;
+    const int64_t nseg = (g.M + L - 1) / L;
+    // auto: the fix-up reaches up to -110 / ln(coef) steps into a segment (the
+    // decay product underflows there); keep that under a quarter of it.
+    const VrowsSpec v = VSpec<P>::get(p);
+    int64_t min_len = kVrowsMinLen;
+    if (v.coef > 0.f && v.coef < 1.f) min_len = std::max(min_len, (int64_t)(4.0 * -110.0 / std::log((double)v.coef)));
+    if ((!forced && L < min_len) || L > 0x7fffffffLL) return Flat3L<P>::run(p, g, ws, wsb, s);
+    // The segment words live in the stream's workspace across three launches,
+    // enqueued under the caller's launch lock.
+    float* seg_a = reinterpret_cast<float*>(static_cast<char*>(ws) + 64);
+    float* seg_b = seg_a + nseg;
+    float* carry = seg_b + nseg;
+    int* code = reinterpret_cast<int*>(carry + nseg);
+    vseg_kernel<P><<<(unsigned)((nseg + 3) / 4), 128, 0, s>>>(p, g, L, nseg, v.coef, seg_a, seg_b, code);
+    if (cudaPeekAtLastError() != cudaSuccess) return RLS_ECUDA;
+    return vrows_finish(v.alg, v.f0, v.f1, sizeof(typename P::InT) == 2, p.out0, g.M, g.S, v.coef, v.ends_at, seg_a,
+                        seg_b, carry, code, nseg, L, s);
+  }
+}
+template <class P>
+struct VrowsL {
+  static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
+    return launch_vrows<P>(p, g, ws, wsb, s, path_mode() == 8);
+  }
+};
+
 // flat2 tiles: R rounds of 32 lanes x one 16-byte vector (RLS_FLAT2_R = 1, 2, 4).
 template <class P>
 struct Flat2L {
@@ -439,9 +548,10 @@ int family(const Geom& g) {
   if (m == 5) return rows_ok ? 5 : 3;
   if (m == 6) return rows_ok ? 6 : 3;
   if (m == 7) return rows_ok ? 7 : 3;
+  if (m == 8) return rows_ok ? 8 : 3;
   if (m != 0) return 0;
   if (rows_ok && g.N >= kRowsMinEnvs) return 4;
-  return rows_ok ? 6 : 3;
+  return rows_ok ? 8 : 3;  // virtual rows where the policy and the length allow, else flat3
 }
 
 template <class Alg, int MAXR = 4>
@@ -475,6 +585,16 @@ int make_geom(int64_t N, int64_t T, const rls_segment_t* seg, bool backward, Geo
 }
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Every call enqueues its launches under one process-wide lock.  A call may
+// take several launches that share the stream's workspace (a look-back kernel
+// and the epoch advance after it; the three virtual-row launches), and host
+// threads that share a stream must not interleave those sequences.  Only the
+// enqueue is serialised (microseconds), never the GPU work.
+std::recursive_mutex& launch_mutex() {
+  static std::recursive_mutex mu;
+  return mu;
+}
 
 bool valid_dtype(int d) { return d == RLS_F32 || d == RLS_BF16; }
 
@@ -545,6 +665,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
   int st = make_geom(num_envs, seq_len, seg, true, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
   const float gl = gamma * lambda_;
 #define GAE_PARAMS(T)                                                                                     \
   typename GaeAlg<T>::Params p;                                                                           \
@@ -563,6 +684,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       if (fam == 5) return gae_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return gae_v<Flat3L, float>(p, g, ws, ws_bytes, s);
       if (fam == 7) return gae_v<Flat4L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return gae_v<VrowsL, float>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -574,6 +696,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
       if (fam == 5) return gae_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return gae_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 7) return gae_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return gae_v<VrowsL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<GaeAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -598,6 +721,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
   int st = make_geom(num_envs, seq_len, nullptr, true, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
 #define VT_PARAMS(T)                                                                                      \
   typename VtraceAlg<T>::Params p;                                                                        \
   p.lpt = (const T*)log_pi_target; p.lpb = (const T*)log_pi_behavior; p.v = (const T*)values;              \
@@ -615,6 +739,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       if (fam == 5) return vtrace_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return vtrace_v<Flat3L, float>(p, g, ws, ws_bytes, s);
       if (fam == 7) return vtrace_v<Flat4L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return vtrace_v<VrowsL, float>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<float>, 2>(p, g, ws, ws_bytes, s);
   } else {
@@ -626,6 +751,7 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       if (fam == 5) return vtrace_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return vtrace_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 7) return vtrace_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return vtrace_v<VrowsL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<VtraceAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -649,6 +775,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   int st = make_geom(num_envs, seq_len, nullptr, true, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
   RetraceAlg::Params p;
   p.pi = action_probs_target; p.mu = action_probs_behavior; p.q = q_values; p.nq = next_q_values_all;
   p.act = actions; p.r = rewards; p.term = terminateds; p.trunc = truncateds;
@@ -698,6 +825,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
   int st = make_geom(num_envs, seq_len, seg, true, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
 #define LAM_PARAMS(T)                                                                                     \
   typename LambdaAlg<T>::Params p;                                                                        \
   p.r = (const T*)rewards; p.nv = (const T*)next_values; p.term = (const T*)terminateds;                   \
@@ -712,6 +840,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       if (fam == 5) return lambda_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return lambda_v<Flat3L, float>(p, g, ws, ws_bytes, s);
       if (fam == 7) return lambda_v<Flat4L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return lambda_v<VrowsL, float>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -723,6 +852,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
       if (fam == 5) return lambda_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return lambda_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 7) return lambda_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return lambda_v<VrowsL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<LambdaAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -745,6 +875,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
   int st = make_geom(num_envs, seq_len, seg, true, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
 #define DISC_PARAMS(T)                                                                                    \
   typename DiscountedAlg<T>::Params p;                                                                    \
   p.r = (const T*)rewards; p.term = (const T*)terminateds; p.trunc = (const T*)truncateds;                 \
@@ -758,6 +889,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       if (fam == 5) return discounted_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return discounted_v<Flat3L, float>(p, g, ws, ws_bytes, s);
       if (fam == 7) return discounted_v<Flat4L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return discounted_v<VrowsL, float>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -769,6 +901,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
       if (fam == 5) return discounted_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return discounted_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 7) return discounted_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return discounted_v<VrowsL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<DiscountedAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -786,6 +919,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
   int st = make_geom(num_envs, seq_len, seg, false, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
 #define FWD_PARAMS(T)                                                                                     \
   typename ForwardAlg<T>::Params p;                                                                       \
   p.x = (const T*)x; p.done = (const T*)dones; p.seed = seed; p.halo = seg ? seg->halo : nullptr;          \
@@ -799,6 +933,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       if (fam == 5) return forward_v<Flat2L, float>(p, g, ws, ws_bytes, s);
       if (fam == 6) return forward_v<Flat3L, float>(p, g, ws, ws_bytes, s);
       if (fam == 7) return forward_v<Flat4L, float>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return forward_v<VrowsL, float>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<float>>(p, g, ws, ws_bytes, s);
   } else {
@@ -810,6 +945,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
       if (fam == 5) return forward_v<Flat2L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 6) return forward_v<Flat3L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
       if (fam == 7) return forward_v<Flat4L, __nv_bfloat16>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return forward_v<VrowsL, __nv_bfloat16>(p, g, ws, ws_bytes, s);
     }
     return launch<ForwardAlg<__nv_bfloat16>, 2>(p, g, ws, ws_bytes, s);
   }
@@ -840,6 +976,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
   int st = make_geom(num_envs, seq_len, seg, direction == 0, g);
   if (st) return st;
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
   if (direction == 0) {
     AffineAlg<true>::Params p{u, v, carry, out, nullptr};
     {
@@ -849,6 +986,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       if (fam == 5) return affine_v<Flat2L, true>(p, g, ws, ws_bytes, s);
       if (fam == 6) return affine_v<Flat3L, true>(p, g, ws, ws_bytes, s);
       if (fam == 7) return affine_v<Flat4L, true>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return affine_v<VrowsL, true>(p, g, ws, ws_bytes, s);
     }
     return launch<AffineAlg<true>>(p, g, ws, ws_bytes, s);
   }
@@ -860,6 +998,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
       if (fam == 5) return affine_v<Flat2L, false>(p, g, ws, ws_bytes, s);
       if (fam == 6) return affine_v<Flat3L, false>(p, g, ws, ws_bytes, s);
       if (fam == 7) return affine_v<Flat4L, false>(p, g, ws, ws_bytes, s);
+      if (fam == 8) return affine_v<VrowsL, false>(p, g, ws, ws_bytes, s);
     }
   return launch<AffineAlg<false>>(p, g, ws, ws_bytes, s);
 }
@@ -907,6 +1046,7 @@ extern "C" int rls_gae_noalloc(const void* rewards, const void* values, const vo
     ws = g_noalloc_ptr[dev];
   }
   cudaStream_t s = as_stream(stream);
+  std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
   // Ticket and exit counters (bytes 0-7) and the error latch (12-15); the
   // epoch (8-11) must keep counting up.
   if (cudaMemsetAsync(ws, 0, 8, s) != cudaSuccess) return RLS_ECUDA;

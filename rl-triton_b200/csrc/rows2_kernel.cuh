@@ -850,4 +850,93 @@ __global__ void __launch_bounds__(WPB * 32) flat4_kernel(const typename P::Param
   if (err && lane == 0) atomicOr(&ws.hdr->error, err);
 }
 
+// ===========================================================================
+// vseg: virtual rows.  The flat buffer is cut into nseg segments of L steps
+// (L a multiple of the chunk), each scanned by one warp in one walk -- the
+// lean row kernel's loop over a flat range -- with carry 0 at its entry.  Real
+// row edges inside a segment are handled as everywhere else (b = 0), and the
+// neighbour across the entry cut is read from memory, so only the carry is
+// missing; each segment leaves its map (A = state at the far end, B = product
+// of b) for the carry composition and the bounded fix-up in segment.cu, and a
+// fix-up code.  With binary flags every b is 0 or the constant bcoef (gamma,
+// gamma*lambda, or 1 for the prefix sum), so the decay product k steps in is
+// bcoef^(k+1) up to the first b = 0: the code is that element's offset from
+// the segment start (-1 if the segment has none) and the fix-up needs no flag
+// reads.  Any other b gives -2 (the fix-up walks the decay product).
+// ===========================================================================
+template <class P>
+__global__ void __launch_bounds__(128) vseg_kernel(const typename P::Params p, const Geom g, int64_t L, int64_t nseg,
+                                                   float bcoef, float* seg_a, float* seg_b, int* seg_code) {
+  using CS = ChunkScan<P, 1>;
+  constexpr int VEC = CS::VEC;
+  constexpr int64_t CH = 32 * VEC;
+  constexpr bool BWD = P::kBackward;
+  constexpr unsigned FULL = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int64_t sidx = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (sidx >= nseg) return;
+  const int64_t s0 = sidx * L;
+  const int64_t len = (g.M - s0 < L) ? g.M - s0 : L;
+  const int64_t nch = (len + CH - 1) / CH;
+  auto cbase = [&](int64_t k) { return s0 + (BWD ? (nch - 1 - k) : k) * CH; };
+  using Nbr = typename P::Nbr;
+  Nbr nb{};
+  if constexpr (P::kNeedsNbr) {
+    const int64_t gn = BWD ? s0 + len : s0 - 1;
+    if (BWD ? (gn < g.M) : (gn >= 0)) nb = P::nbr_global(p, gn);
+  }
+  int code = -1;
+  bool binary = true;  // every b seen so far is 0 or bcoef
+  // First b = 0 of the chunk in walk order (called until one is found).
+  auto first_zero = [&](const CS& cs, int64_t cb) {
+    int q0 = VEC;
+#pragma unroll
+    for (int q = 0; q < VEC; ++q) {
+      const int e = BWD ? VEC - 1 - q : q;
+      const float c = cs.cb[0][e];
+      binary = binary && (c == 0.f || c == bcoef);
+      if (c == 0.f && q0 == VEC) q0 = q;
+    }
+    const unsigned m = __ballot_sync(FULL, q0 < VEC);
+    if (m) {
+      const int wl = BWD ? 31 - __clz(m) : __ffs(m) - 1;
+      const int qq = __shfl_sync(FULL, q0, wl);
+      code = (int)(cb + wl * VEC + (BWD ? VEC - 1 - qq : qq) - s0);
+    }
+  };
+  RowCursor cur;
+  Pair M = pair_identity();
+  float carry = 0.f;
+  Rows2Chunk<P, 1> a, b;
+  flat_load<P, 1, true>(p, g.M, cbase(0), lane, a);
+#pragma unroll 1
+  for (int64_t k = 0; k < nch; k += 2) {
+    if (k + 1 < nch) flat_load<P, 1, true>(p, g.M, cbase(k + 1), lane, b);
+    {
+      CS cs;
+      flat_chunk_setup<P, 1>(g, cbase(k), lane, k == 0, cur, cs);
+      nb = cs.pass1(p, g, lane, a, nb);
+      if (code == -1) first_zero(cs, cbase(k));
+      M = compose(cs.aggregate(), M);
+      carry = cs.pass2(p, g, a, carry);
+    }
+    if (k + 1 >= nch) break;
+    if (k + 2 < nch) flat_load<P, 1, true>(p, g.M, cbase(k + 2), lane, a);
+    {
+      CS cs;
+      flat_chunk_setup<P, 1>(g, cbase(k + 1), lane, false, cur, cs);
+      nb = cs.pass1(p, g, lane, b, nb);
+      if (code == -1) first_zero(cs, cbase(k + 1));
+      M = compose(cs.aggregate(), M);
+      carry = cs.pass2(p, g, b, carry);
+    }
+  }
+  if (!__all_sync(FULL, binary)) code = -2;
+  if (lane == 0) {
+    seg_a[sidx] = carry;
+    seg_b[sidx] = M.b;
+    seg_code[sidx] = code;
+  }
+}
+
 }  // namespace rls

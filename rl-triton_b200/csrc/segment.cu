@@ -216,7 +216,196 @@ int fill_args(int alg, const void* flag0, const void* flag1, int in_dtype, int64
   return RLS_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Virtual rows (one long buffer cut into nseg segments of L steps, scanned with
+// carry 0 at each segment's entry by vseg_kernel): compose the carries in walk
+// order, then add P[t] * carry from each segment's entry inward until P is 0.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void flat_row_col(int64_t i, int64_t S, int64_t& row, int64_t& col) {
+  if (i < 0x7fffffffLL && S < 0x7fffffffLL) {
+    const unsigned q = (unsigned)i / (unsigned)S;
+    row = q;
+    col = i - (int64_t)q * S;
+  } else {
+    row = i / S;
+    col = i - row * S;
+  }
+}
+
+// Decay of flat element i inside a virtual-row walk: 0 at the edge of a (local)
+// row on the side the carry enters from, else the recurrence's b.
+__device__ float vrow_decay(const SegArgs& a, int64_t i) {
+  int64_t row, col;
+  flat_row_col(i, a.S, row, col);
+  if (a.backward ? (col == a.S - 1) : (col == 0)) return 0.f;
+  return decay_at(a, row, col);
+}
+
+// One block: the maps are staged in shared memory (coalesced), then warp 0
+// composes each lane's run serially, scans across the runs with shuffles and
+// re-walks its run, leaving the carries in place of the A's; all threads then
+// store them coalesced.
+constexpr int kCarryThreads = 1024;
+__global__ void __launch_bounds__(kCarryThreads) vrows_carry(const float* seg_a, const float* seg_b, float* carry,
+                                                             int64_t nseg, int backward) {
+  extern __shared__ float sm[];  // [nseg] a (then the carries), [nseg] b
+  float* sa = sm;
+  float* sb = sm + nseg;
+  for (int64_t i = threadIdx.x; i < nseg; i += kCarryThreads) {
+    sa[i] = seg_a[i];
+    sb[i] = seg_b[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    const int64_t run = (nseg + 31) / 32;
+    const int64_t w0 = lane * run, w1 = (w0 + run < nseg) ? w0 + run : nseg;
+    auto seg_of = [&](int64_t w) { return backward ? nseg - 1 - w : w; };
+    Pair m = pair_identity();
+    for (int64_t w = w0; w < w1; ++w) {
+      const int64_t sg = seg_of(w);
+      m = compose(Pair{sa[sg], sb[sg]}, m);
+    }
+    Pair incl = m;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const Pair o{__shfl_up_sync(0xffffffffu, incl.a, d), __shfl_up_sync(0xffffffffu, incl.b, d)};
+      if (lane >= d) incl = compose(incl, o);
+    }
+    float c = __shfl_up_sync(0xffffffffu, incl.a, 1);
+    if (lane == 0) c = 0.f;
+    for (int64_t w = w0; w < w1; ++w) {
+      const int64_t sg = seg_of(w);
+      const float next = fmaf(sb[sg], c, sa[sg]);
+      sa[sg] = c;  // now the carry entering segment sg
+      c = next;
+    }
+  }
+  __syncthreads();
+  for (int64_t i = threadIdx.x; i < nseg; i += kCarryThreads) carry[i] = sa[i];
+}
+
+// Block per segment.  Code >= -1 (binary flags: b is 0 or coef): the decay
+// product k steps in from the entry is coef^(k+1) up to the first b = 0 and
+// underflows to 0 within ~-104/ln(coef) steps, so the carry is applied over
+// that range with no flag reads, eight loads in flight per thread before
+// their stores.  Code -2: 2048 walk-order steps per pass with a block product
+// scan until P is 0.  Either way the block clears the segment's four words.
+constexpr int kFixBatch = 8;
+__global__ void __launch_bounds__(kBlockWalk) vrows_fixup(const SegArgs a, int64_t L, float* seg_a, float* seg_b,
+                                                          float* carry, int* seg_code) {
+  constexpr int NW = kBlockWalk / 32;
+  constexpr int STEP = kBlockWalk * kBlockElems;
+  __shared__ float s_w[NW];
+  __shared__ float s_base;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t sg = blockIdx.x;
+  const float c = carry[sg];
+  const int code = seg_code[sg];
+  __syncthreads();  // every thread has read its words before they are cleared
+  if (threadIdx.x == 0) {
+    seg_a[sg] = 0.f;
+    seg_b[sg] = 0.f;
+    carry[sg] = 0.f;
+    seg_code[sg] = 0;
+  }
+  if (c == 0.f) return;  // uniform across the block
+  const int64_t s0 = sg * L;
+  const int64_t len = (a.N - s0 < L) ? a.N - s0 : L;  // a.N holds the flat length here
+  if (code >= -1) {
+    int64_t n = code >= 0 ? (a.backward ? len - 1 - code : code) : len;  // steps that take the carry
+    const bool unit = a.coef == 1.f;
+    if (!unit) {
+      const float lim = a.coef > 0.f && a.coef < 1.f ? -110.f / logf(a.coef) + 64.f : 0.f;
+      if ((float)n > lim) n = (int64_t)lim;
+    }
+    for (int64_t k0 = 0; k0 < n; k0 += (int64_t)kBlockWalk * kFixBatch) {
+      float v[kFixBatch];
+      int64_t idx[kFixBatch];
+#pragma unroll
+      for (int j = 0; j < kFixBatch; ++j) {
+        const int64_t k = k0 + (int64_t)j * kBlockWalk + threadIdx.x;  // walk distance from the entry
+        idx[j] = k < n ? (a.backward ? s0 + len - 1 - k : s0 + k) : -1;
+        v[j] = idx[j] >= 0 ? a.out[idx[j]] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < kFixBatch; ++j) {
+        if (idx[j] < 0) continue;
+        const int64_t k = k0 + (int64_t)j * kBlockWalk + threadIdx.x;
+        const float P = unit ? 1.f : powf(a.coef, (float)(k + 1));
+        a.out[idx[j]] = fmaf(P, c, v[j]);
+      }
+    }
+    return;
+  }
+  float base = 1.f;
+  for (int64_t k0 = 0; k0 < len; k0 += STEP) {
+    float b[kBlockElems];
+    int64_t idx[kBlockElems];
+#pragma unroll
+    for (int q = 0; q < kBlockElems; ++q) {
+      const int64_t k = k0 + (int64_t)threadIdx.x * kBlockElems + q;
+      idx[q] = k < len ? (a.backward ? s0 + len - 1 - k : s0 + k) : -1;
+      b[q] = idx[q] >= 0 ? vrow_decay(a, idx[q]) : 1.f;
+    }
+    float mine = 1.f;
+#pragma unroll
+    for (int q = 0; q < kBlockElems; ++q) mine *= b[q];
+    float incl = mine;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl *= o;
+    }
+    if (lane == 31) s_w[warp] = incl;
+    __syncthreads();
+    float before = 1.f, total = 1.f;
+    for (int w = 0; w < NW; ++w) {
+      if (w == warp) before = total;
+      total *= s_w[w];
+    }
+    const float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    float P = base * before * (lane == 0 ? 1.f : excl);
+#pragma unroll
+    for (int q = 0; q < kBlockElems; ++q) {
+      P *= b[q];
+      if (idx[q] >= 0 && P != 0.f) a.out[idx[q]] = fmaf(P, c, a.out[idx[q]]);
+    }
+    if (threadIdx.x == 0) s_base = base * total;
+    __syncthreads();
+    base = s_base;
+    __syncthreads();  // s_w / s_base are rewritten next pass
+    if (base == 0.f) break;  // uniform
+  }
+}
+
 }  // namespace
+
+namespace rls {
+
+int vrows_finish(int alg, const void* f0, const void* f1, int bf16, float* out, int64_t M, int64_t S, float coef,
+                 int ends_at, float* seg_a, float* seg_b, float* carry, int* seg_code, int64_t nseg, int64_t L,
+                 cudaStream_t s) {
+  SegArgs a{};
+  a.alg = alg;
+  a.f0 = f0;
+  a.f1 = f1;
+  a.bf16 = bf16;
+  a.out = out;
+  a.N = M;
+  a.S = S;
+  a.coef = coef;
+  a.ends_at = ends_at;
+  a.halo = nullptr;
+  a.backward = !(alg == RLS_ALG_ELIGIBILITY || alg == RLS_ALG_PREFIX || alg == RLS_ALG_SCAN_FWD);
+  const size_t smem = (size_t)nseg * 2 * sizeof(float);
+  if (smem > 48 * 1024) return RLS_EINVAL;  // callers keep nseg <= 6144
+  vrows_carry<<<1, kCarryThreads, smem, s>>>(seg_a, seg_b, carry, nseg, a.backward);
+  vrows_fixup<<<(unsigned)nseg, kBlockWalk, 0, s>>>(a, L, seg_a, seg_b, carry, seg_code);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+}
+
+}  // namespace rls
 
 extern "C" {
 

@@ -33,7 +33,7 @@ def T(a, dev="cuda", dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)
 
 
-@pytest.fixture(autouse=True, params=["auto", "rows2", "flat3", "flat2", "tile", "rows", "flat"])
+@pytest.fixture(autouse=True, params=["auto", "rows2", "vrows", "flat3", "flat2", "tile", "rows", "flat"])
 def kernel_path(request, monkeypatch):
     """Run every case on each kernel family: the library's own choice ("auto"),
     the TMA-staged tile kernel, the row-parallel register kernel (one warp per
@@ -323,7 +323,7 @@ def test_kernel_families_share_one_workspace():
     from rl_triton import _native as nat
     old = os.environ.get("RLS_PATH")
     try:
-        for path in ["flat3", "flat2", "tile", "flat3", "flat", "flat2", "flat3", "tile", "flat2"]:
+        for path in ["vrows", "flat3", "flat2", "tile", "vrows", "flat", "flat2", "flat3", "vrows", "tile", "flat2"]:
             os.environ["RLS_PATH"] = path
             for n, t in [(64, 512), (1, 4095), (3, 5000)]:
                 x = rng_inputs(n, t, seed=n + t)
@@ -336,3 +336,40 @@ def test_kernel_families_share_one_workspace():
             os.environ.pop("RLS_PATH", None)
         else:
             os.environ["RLS_PATH"] = old
+
+
+def _no_less_accurate(got, oracle, msg):
+    """Within rtol / atol of the fp32 sequential oracle or, where cutting a
+    running sum over 10^4-10^5-step episodes reassociates it, no less accurate
+    than that fp32 reference: the worst error against the fp64 oracle at most
+    twice the fp32 reference's own worst error, plus atol."""
+    w32 = oracle("f32")
+    if np.all(np.abs(got - w32) <= ATOL + RTOL * np.abs(w32)):
+        return
+    w64 = oracle("f64")
+    ours, ref = float(np.max(np.abs(got - w64))), float(np.max(np.abs(w32 - w64)))
+    assert ours <= 2 * ref + ATOL, f"{msg}: max error vs fp64 {ours}, fp32 reference's {ref}"
+
+
+def test_virtual_row_fixup_paths(kernel_path):
+    """Virtual rows on long rows: the flag-free fix-up (prefix sums over binary
+    dones, episodes longer than a segment, so some segments hold no reset at
+    all), the product-walk fix-up (fractional dones, decaying traces, GAE), both
+    scan directions and a row count that does not divide the segments."""
+    if kernel_path != "vrows":
+        pytest.skip("runs once, with RLS_PATH=vrows")
+    import rl_triton
+    g = np.random.default_rng(77)
+    for n, t in [(1, 1 << 20), (3, 300032)]:
+        x = rng_inputs(n, t, seed=n, p_done=2e-5)
+        for bd in ["ends_at", "starts_at"]:
+            got = rl_triton.compute_episodic_prefix_sum(T(x["r"]), T(x["term"]), boundary=bd).cpu().numpy()
+            _no_less_accurate(got, lambda pr: orc.prefix_sum(x["r"], x["term"], None, bd == "ends_at", precision=pr),
+                              f"prefix {bd} {n}x{t}")
+        frac = np.where(g.random((n, t)) < 1e-4, 0.5, x["term"]).astype(np.float32)
+        got = rl_triton.compute_episodic_prefix_sum(T(x["r"]), T(frac)).cpu().numpy()
+        _no_less_accurate(got, lambda pr: orc.prefix_sum(x["r"], frac, precision=pr), f"prefix fractional {n}x{t}")
+        got = rl_triton.compute_eligibility_traces(T(x["r"]), T(x["term"]), 0.99, 0.95).cpu().numpy()
+        close(got, orc.eligibility_traces(x["r"], x["term"], 0.99, 0.95), msg=f"traces {n}x{t}")
+        got = rl_triton.compute_gae(T(x["r"]), T(x["v"]), T(x["term"]), gamma=0.99, lambda_=0.95).cpu().numpy()
+        close(got, orc.gae(x["r"], x["v"], x["term"]), msg=f"gae {n}x{t}")
