@@ -521,7 +521,8 @@ def run_b200(args, world, rank, local):
                "sample": sample + "; oracle/rlscan_oracle.c (CPU restatement of the reference's sequential "
                                   "estimators), rows split over host threads"}
 
-    n_launch = len(cfg["funcs"]) * args.steps
+    n_launch = launches_per_step(calls[0], stream)
+    n_launch = n_launch * args.steps if n_launch is not None else len(cfg["funcs"]) * args.steps
     if rank == 0:
         line = {
             "metric": "timesteps/sec", "value": value, "unit": "timesteps/s", "n_gpus": world,
@@ -562,6 +563,27 @@ def run_ncu(args, local):
         for f in calls.values():
             f()
     torch.cuda.synchronize(dev)
+
+
+def launches_per_step(calls, stream):
+    """Kernels of this library launched by one eager step, counted by the CUDA
+    profiler in an untimed pass (library kernels live in namespace rls or are
+    the epoch / segment helpers; PyTorch's own kernels and copies are not
+    counted).  None when the profiler is unavailable."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            with torch.cuda.stream(stream):
+                for f in calls.values():
+                    f()
+            stream.synchronize()
+        names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+        ours = [n for n in names if "at::" not in n and not n.startswith(("Memcpy", "Memset", "nccl", "ncclDevKernel"))
+                and ("rls::" in n or "advance_epoch" in n or "vrows_" in n or "segment_walk" in n or "_kernel" in n)]
+        return len(ours) or None
+    except Exception:  # noqa: BLE001
+        return None
 
 
 def _used(key, cfg):
