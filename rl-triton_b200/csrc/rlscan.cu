@@ -391,7 +391,7 @@ namespace {
 // ---- virtual rows -------------------------------------------------------------
 // Scans whose output is the state itself (GAE, lambda and discounted returns,
 // eligibility traces, prefix sums) on few long rows: cut the flat buffer into
-// ~32 segments per SM, scan each with carry 0 in one walk (vseg_kernel: no
+// one resident warp's worth of segments per SM slot, scan each with carry 0 in one walk (vseg_kernel: no
 // second pass, no look-back), then compose the carries and apply the bounded
 // fix-up out[t] += P[t] * carry (vrows_finish), which touches each segment
 // only up to its first reset (or until P underflows).  Auto picks it when the
@@ -437,7 +437,7 @@ struct VSpec<ForwardT<T, PREV>> {
   }
 };
 
-constexpr int64_t kVrowsSegs = 32 * 148;  // segments: 32 warps per SM
+constexpr int64_t kVrowsSegs = 32 * 148;  // segments if the occupancy query fails: 32 warps per SM
 constexpr int64_t kVrowsMinLen = 16384;   // auto: shortest segment worth its fix-up
 
 // forced (RLS_PATH=vrows): any length; auto: only when segments reach
@@ -449,9 +449,22 @@ int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t ws
     return Flat3L<P>::run(p, g, ws, wsb, s);
   } else {
     if (g.M == 0) return RLS_OK;
-    // segments: kVrowsSegs, or as many as the workspace holds (four words each)
+    // segments: one full wave of vseg_kernel (4 warps per block, resident blocks
+    // per SM from its register count x the SMs), or as many as the workspace
+    // holds (four words each).  A partial second wave would leave most SMs idle
+    // at the end.
+    static int64_t wave = 0;  // per instantiation; racing first calls compute the same value
+    if (wave == 0) {
+      int nb = 0, dev = 0, sms = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, vseg_kernel<P>, 128, 0) != cudaSuccess ||
+          cudaGetDevice(&dev) != cudaSuccess ||
+          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || nb < 1 || sms < 1)
+        wave = kVrowsSegs;
+      else
+        wave = std::min<int64_t>((int64_t)nb * 4 * sms, 6144);  // vrows_carry stages <= 6144 maps
+    }
     const int64_t room = ws && wsb > 64 ? (int64_t)((wsb - 64) / 16) : 0;
-    const int64_t want = room < kVrowsSegs ? room : kVrowsSegs;
+    const int64_t want = room < wave ? room : wave;
     if (want < 1) return Flat3L<P>::run(p, g, ws, wsb, s);
     int64_t L = (g.M + want - 1) / want;
     L = (L + CH - 1) / CH * CH;
