@@ -291,28 +291,19 @@ int launch_flat3(const typename P::Params& p, const Geom& g0, void* ws, size_t w
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   g.ws_cap = ws ? packed_capacity(wsb) : 0;
   if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
-  g.l2_prefetch = env_int("RLS_FLAT3_PF", 0);
+  g.l2_prefetch = 0;  // the bulk L2 prefetch measured within noise; kept off
   flat3_kernel<P, NCH, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
   advance_epoch<<<1, 1, 0, s>>>(ws);
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
 }
 
-// Super-tiles of RLS_FLAT3_STEPS steps (1024, 2048, 4096; default 2048) in
-// chunks of one 16-byte vector per lane (two vectors per lane measured slower:
-// the extra registers cost more warps than the deeper loads gain).
+// Super-tiles of 2048 steps in chunks of one 16-byte vector per lane (sweeps of
+// 1024-4096 steps and of two vectors per lane measured no better).
 template <class P>
 struct Flat3L {
-  template <int R>
-  static int go(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, int steps) {
-    constexpr int kChunk = 32 * R * (16 / (int)sizeof(typename P::InT));
-    const int nch = steps / kChunk;
-    if (nch <= 4) return launch_flat3<P, 4, R>(p, g, ws, wsb, s);
-    if (nch <= 8) return launch_flat3<P, 8, R>(p, g, ws, wsb, s);
-    return launch_flat3<P, 16, R>(p, g, ws, wsb, s);
-  }
   static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
-    const int steps = env_int("RLS_FLAT3_STEPS", 2048);
-    return go<1>(p, g, ws, wsb, s, steps);
+    constexpr int kChunk = 32 * (16 / (int)sizeof(typename P::InT));
+    return launch_flat3<P, 2048 / kChunk, 1>(p, g, ws, wsb, s);
   }
 };
 
@@ -346,34 +337,14 @@ int launch_flat4(const typename P::Params& p, const Geom& g0, void* ws, size_t w
   }
 }
 
-// flat4: RLS_FLAT3_STEPS per super-tile as flat3; RLS_FLAT4_D ring slots (3 or
-// 4); RLS_FLAT4_EPL steps per lane and chunk (8 or 16; rows must be a multiple).
+// flat4: 2048-step super-tiles, a 4-slot ring, one vector per lane and chunk (the
+// kernel's other options -- resident super-tile, contiguous per-lane runs --
+// measured no better and are not instantiated).
 template <class P>
 struct Flat4L {
-  static constexpr int V0 = 16 / (int)sizeof(typename P::InT);
-  template <int D, int G>
-  static int go(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, int steps) {
-    constexpr int kChunk = 32 * V0 * G;
-    const int nch = steps / kChunk;
-    if (nch <= 4) return launch_flat4<P, 4, D, G>(p, g, ws, wsb, s);
-    if (nch <= 8) return launch_flat4<P, 8, D, G>(p, g, ws, wsb, s);
-    return launch_flat4<P, 16, D, G>(p, g, ws, wsb, s);
-  }
-  template <int G>
-  static int d(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, int steps) {
-    const int dd = env_int("RLS_FLAT4_D", 4);
-    if (dd == 0) return go<0, G>(p, g, ws, wsb, s, steps);
-    return dd == 3 ? go<3, G>(p, g, ws, wsb, s, steps) : go<4, G>(p, g, ws, wsb, s, steps);
-  }
   static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
-    const int steps = env_int("RLS_FLAT3_STEPS", 2048);
-    const int epl = env_int("RLS_FLAT4_EPL", 16);
-    int gsel = epl / V0;
-    if (gsel > 4) gsel = 4;
-    while (gsel > 1 && g.S % (V0 * gsel) != 0) gsel /= 2;
-    if (gsel >= 4) return d<4>(p, g, ws, wsb, s, steps);
-    if (gsel == 2) return d<2>(p, g, ws, wsb, s, steps);
-    return d<1>(p, g, ws, wsb, s, steps);
+    constexpr int kChunk = 32 * (16 / (int)sizeof(typename P::InT));
+    return launch_flat4<P, 2048 / kChunk, 4, 1>(p, g, ws, wsb, s);
   }
 };
 
@@ -494,13 +465,10 @@ struct VrowsL {
   }
 };
 
-// flat2 tiles: R rounds of 32 lanes x one 16-byte vector (RLS_FLAT2_R = 1, 2, 4).
+// flat2 tiles: 4 rounds of 32 lanes x one 16-byte vector (512 fp32 steps).
 template <class P>
 struct Flat2L {
   static int run(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s) {
-    const int r = env_int("RLS_FLAT2_R", 4);
-    if (r == 1) return launch_flat2<P, 1>(p, g, ws, wsb, s);
-    if (r == 2) return launch_flat2<P, 2>(p, g, ws, wsb, s);
     return launch_flat2<P, 4>(p, g, ws, wsb, s);
   }
 };
