@@ -18,6 +18,18 @@ input set; the input sets rotate so the working set exceeds the 126 MB L2
 Under torchrun (N > 1) every rank runs the same per-GPU workload on its own
 environments (env-sharded, weak scaling, no collective in the data path).
 
+After the timed region, and outside it:
+  * per function, the device time per launch (graph replay) and the eager
+    full-call time through the public API;
+  * parity: every output of the first input set against the fp32 C oracle
+    (oracle/, test infrastructure) at rtol = atol = 1e-5 -> "parity";
+  * the reference's own Triton kernels (the unmodified package installed under
+    baseline/_ref, run in a child process that never imports this repository's
+    package) on the same inputs, rotation and timing -> "triton_reference",
+    with the largest output difference against this arm;
+  * end to end through the public API from pinned host buffers -> "e2e";
+  * the CPU baseline (the C oracle on the host cores) -> "cpu_baseline".
+
 `--impl reference` times the CPU restatement of the reference's sequential
 estimators (oracle/, all host threads) on the same workload; rank 0 prints.
 """
@@ -32,8 +44,15 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(ROOT, "rl-triton_b200"))
-sys.path.insert(0, ROOT)
+REF_INSTALL = os.path.join(ROOT, "baseline", "_ref")  # the unmodified reference (pip --target), not in git
+TRITON_WORKER = "--triton-worker" in sys.argv
+if TRITON_WORKER:
+    # The reference's own Triton kernels, imported from its install: this
+    # process never puts this repository's package or library on its path.
+    sys.path.insert(0, REF_INSTALL)
+elif os.path.join(ROOT, "rl-triton_b200") not in sys.path:
+    sys.path.insert(0, os.path.join(ROOT, "rl-triton_b200"))
+sys.path.insert(1 if TRITON_WORKER else 0, ROOT)
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -75,7 +94,7 @@ CONFIGS = {
 
 # --------------------------------------------------------------------------
 def make_inputs(cfg, device, seed, gen_device=None):
-    """Seeded synthetic inputs (distributions of BASELINE configs 2-5)."""
+    """Seeded synthetic inputs with the distributions of the headline metric's configurations 2-5."""
     N, T = cfg["N"], cfg["T"]
     g = torch.Generator(device=device).manual_seed(seed)
     dt = torch.bfloat16 if cfg["bf16"] else torch.float32
@@ -114,9 +133,10 @@ def make_inputs(cfg, device, seed, gen_device=None):
         x["mu"] = pa * torch.exp(-(lt - lb))  # IS ratio pi_a/mu = exp(lt - lb)
         x["q"] = randn(N, T)
         x["nq"] = randn(N, T, A)
-        x["trunc32"] = x["trunc"].float() if cfg["trunc"] else torch.zeros(N, T, device=device)
-        x["term32"] = x["term"].float()
-        x["r32"] = x["r"].float()
+        if not cfg["trunc"]:
+            # Retrace's API always takes truncateds; a workload without
+            # truncations passes zeros (a constant, not per-step data).
+            x["notrunc"] = torch.zeros(N, T, device=device)
     return x
 
 
@@ -144,7 +164,7 @@ def make_calls(cfg, x, split=False):
         x["lpt"], x["lpb"], x["v"], x["r"], x["term"], truncateds=x.get("trunc") if tr else None, gamma=0.99,
         rho_bar=1.0, c_bar=1.0, bootstrap_values=x.get("boot") if tr else None)
     calls["retrace"] = lambda: rl_triton.compute_retrace(
-        x["pi"], x["mu"], x["q"], x["nq"], x["act"], x["r32"], x["term32"], x["trunc32"], gamma=0.99,
+        x["pi"], x["mu"], x["q"], x["nq"], x["act"], x["r"], x["term"], x["trunc"] if tr else x["notrunc"], gamma=0.99,
         lambda_=0.95, c_bar=1.0, rho_bar=1.0)
     calls["lambda"] = lambda: rl_triton.compute_lambda_returns(
         x["r"], x["nv"], x["term"], truncateds=x.get("trunc") if tr else None, gamma=0.99, lambda_=0.95,
@@ -289,8 +309,9 @@ def cpu_oracle_step(cfg_name, cfg, x_np, nthreads):
                                   x_np.get("trunc") if tr else None, x_np.get("boot") if tr else None,
                                   orc.BOOT_FULL_ADD if tr else orc.BOOT_NONE, nthreads=nthreads))
         elif f == "retrace":
-            out.append(orc.retrace(x_np["pi"], x_np["mu"], x_np["q"], x_np["nq"], x_np["act"], x_np["r32"],
-                                   x_np["term32"], x_np["trunc32"], 0.99, 0.95, nthreads=nthreads))
+            out.append(orc.retrace(x_np["pi"], x_np["mu"], x_np["q"], x_np["nq"], x_np["act"], x_np["r"],
+                                   x_np["term"], x_np["trunc"] if tr else x_np["notrunc"], 0.99, 0.95,
+                                   nthreads=nthreads))
         elif f == "lambda":
             out.append(orc.lambda_returns(x_np["r"], x_np["nv"], x_np["term"], x_np.get("trunc") if tr else None,
                                           x_np.get("boot") if tr else None,
@@ -338,12 +359,31 @@ def cpu_sample(cfg, budget_s=15.0, max_steps=50):
 
 
 # --------------------------------------------------------------------------
+def input_sets(cfg):
+    """Input sets rotated between steps so the working set exceeds the 126 MB L2."""
+    per_set = sum(bytes_per_step(f, cfg["trunc"], cfg["bf16"]) for f in cfg["funcs"]) * cfg["N"] * cfg["T"]
+    n_sets = max(1, min(8, int(np.ceil(3 * 126e6 / per_set)))) if per_set < 3 * 126e6 else 1
+    return n_sets, per_set
+
+
+def config_dict(cfg, world, split, n_sets, per_set, use_graph):
+    """The `config` object of the JSON line; both arms print the same one."""
+    return {"workload": cfg["desc"], "functions": cfg["funcs"], "num_envs_per_gpu": cfg["N"],
+            "seq_len": cfg["T"],
+            "parallelism": (f"time-split x{world}" if split else f"env-sharded x{world}") if world > 1
+            else "single GPU",
+            "l2": f"{n_sets} rotating input sets ({per_set * n_sets / 1e6:.0f} MB > 126 MB L2)",
+            "launch": "CUDA graph per input set" if use_graph else "eager"}
+
+
 def run_reference(args, world, rank):
     cfg = CONFIGS[args.config]
     if rank != 0:
         return
     from oracle import oracle as orc
 
+    split = world > 1 and cfg.get("split", False)
+    n_sets, per_set = input_sets(dict(cfg, T=cfg["T"] // world) if split else cfg)
     sub = dict(cfg)
     if cfg["N"] * cfg["T"] > (1 << 22):
         sub["N"] = max(1, (1 << 22) // cfg["T"]) if cfg["T"] <= (1 << 22) else 1
@@ -362,15 +402,305 @@ def run_reference(args, world, rank):
     line = {
         "impl": "reference", "metric": "timesteps/sec", "value": value, "unit": "timesteps/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded; BASELINE distributions)",
-        "config": {"workload": cfg["desc"], "functions": cfg["funcs"]},
+        "higher_is_better": True, "scaling": "strong" if split else "weak", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded; distributions of the headline configurations)",
+        "config": config_dict(dict(cfg, T=cfg["T"] // world) if split else cfg, world, split, n_sets, per_set,
+                              not split),
         "cpu_baseline": {"value": value, "unit": "timesteps/s", "cores": nth, "kind": "port",
                          "sample": sample + "; CPU restatement of the reference's sequential estimators "
                                             "(oracle/rlscan_oracle.c), rows split over host threads"},
         "e2e": {"value": value, "unit": "timesteps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------
+def time_function(calls, fname, stream, use_graph, min_reps=8, max_reps=200, budget_s=0.5, fixed_reps=0):
+    """Device time per launch of one public call (CUDA graph of `reps` calls over
+    the rotating input sets, CUDA events on the launching stream) and the eager
+    full-call time (the same calls issued from Python, device-resident inputs)."""
+    n_sets = len(calls)
+    with torch.cuda.stream(stream):
+        t0 = time.perf_counter()
+        calls[0][fname]()
+        stream.synchronize()
+        one = time.perf_counter() - t0
+    reps = int(max(min_reps // 2, min(max_reps, budget_s / max(one, 1e-6))))
+    reps = fixed_reps or max(3, reps)  # fixed: ranks must issue the same collectives
+    out = {}
+    g = None
+    if use_graph:
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for k in range(reps):
+                    calls[k % n_sets][fname]()
+        except Exception as e:  # noqa: BLE001
+            g = None
+            out["graph_error"] = f"{type(e).__name__}: {str(e)[:200]}"
+    with torch.cuda.stream(stream):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if g is not None:
+            g.replay()
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+    stream.synchronize()
+    if g is not None:
+        out["us_per_launch"] = round(e0.elapsed_time(e1) * 1e3 / reps, 3)
+        out["launch"] = "graph"
+    del g
+    with torch.cuda.stream(stream):
+        for k in range(reps):
+            calls[k % n_sets][fname]()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        for k in range(reps):
+            calls[k % n_sets][fname]()
+        f1.record(stream)
+    stream.synchronize()
+    out["full_call_us"] = round(f0.elapsed_time(f1) * 1e3 / reps, 3)
+    if "us_per_launch" not in out:
+        out["us_per_launch"] = out["full_call_us"]
+        out["launch"] = "eager"
+    out["reps"] = reps
+    return out
+
+
+def sample_window(cfg):
+    """Rows and columns of an output compared across the two GPU arms."""
+    rows = min(cfg["N"], max(1, (1 << 22) // cfg["T"]))
+    return rows, min(cfg["T"], 1 << 22)
+
+
+def flat_outputs(fname, res):
+    res = res if isinstance(res, tuple) else (res,)
+    return {f"{fname}_{k}": r for k, r in enumerate(res)}
+
+
+def triton_worker(args):
+    """Runs in a child process with only the reference's install on sys.path:
+    times the reference's stock rl_triton.compute_* (Triton JIT for this GPU)
+    on the same inputs, rotation and timing method as the main arm."""
+    import triton
+
+    import rl_triton  # the unmodified reference, from baseline/_ref
+
+    cfg = CONFIGS[args.config]
+    dev = torch.device("cuda", args.device)
+    torch.cuda.set_device(dev)
+    n_sets, _ = input_sets(cfg)
+    sets = []
+    for k in range(n_sets):
+        x = make_inputs(cfg, dev, seed=k)
+        if cfg["bf16"]:  # the reference accepts fp32 only (src/rl_triton/ops/gae.py:109)
+            x = {key: (v.float() if v.dtype == torch.bfloat16 else v) for key, v in x.items()}
+        sets.append(x)
+    calls = [make_calls(cfg, x) for x in sets]
+    stream = torch.cuda.Stream(dev)
+    res = {"module": os.path.relpath(rl_triton.__file__, ROOT), "version": getattr(rl_triton, "__version__", None),
+           "triton": triton.__version__, "inputs": "fp32 copies of the bf16 inputs" if cfg["bf16"] else "same",
+           "per_function": {}}
+    outs = {}
+    rows, cols = sample_window(cfg)
+    for f in cfg["funcs"]:
+        try:
+            with torch.cuda.stream(stream):
+                for c in calls:  # JIT compile + warm-up
+                    c[f]()
+            stream.synchronize()
+            res["per_function"][f] = time_function(calls, f, stream, use_graph=not args.no_graph)
+            with torch.cuda.stream(stream):
+                o = calls[0][f]()
+            stream.synchronize()
+            for key, t in flat_outputs(f, o).items():
+                outs[key] = t[:rows, :cols].float().cpu().numpy()
+        except Exception as e:  # noqa: BLE001
+            res["per_function"][f] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+        torch.cuda.synchronize()
+    if args.triton_out and outs:
+        np.savez(args.triton_out, **outs)
+    print("TRITON_REF_JSON " + json.dumps(res), flush=True)
+
+
+def triton_reference(args, cfg, ours, ours_timing, local):
+    """Launches triton_worker and compares its timings and outputs with this arm's."""
+    import subprocess
+    import tempfile
+
+    if not os.path.isdir(os.path.join(REF_INSTALL, "rl_triton")):
+        return {"reason": "reference not installed under baseline/_ref"}
+    fd, path = tempfile.mkstemp(suffix=".npz")
+    os.close(fd)
+    cmd = [sys.executable, os.path.abspath(__file__), "--triton-worker", "--config", args.config,
+           "--device", str(local), "--triton-out", path]
+    if args.no_graph:
+        cmd.append("--no-graph")
+    env = dict(os.environ)
+    env.pop("PYTHONPATH", None)
+    env.pop("RLS_PATH", None)
+    try:
+        p = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env, cwd="/")
+    except subprocess.TimeoutExpired:
+        return {"reason": "reference worker timed out (900 s)"}
+    line = [ln for ln in p.stdout.splitlines() if ln.startswith("TRITON_REF_JSON ")]
+    if p.returncode != 0 or not line:
+        tail = (p.stderr or p.stdout).strip().splitlines()[-3:]
+        return {"reason": f"reference worker exit {p.returncode}: {' | '.join(tail)[:400]}"}
+    res = json.loads(line[0][len("TRITON_REF_JSON "):])
+    theirs = {}
+    if os.path.exists(path):
+        try:
+            with np.load(path) as z:
+                theirs = {k: z[k] for k in z.files}
+        except Exception:  # noqa: BLE001
+            theirs = {}
+        os.unlink(path)
+    for f, r in res["per_function"].items():
+        if "error" in r:
+            continue
+        mine = ours_timing.get(f, {})
+        r["ours_us"] = mine.get("us_per_launch")
+        r["triton_us"] = r.get("us_per_launch")
+        if r["ours_us"] and r["triton_us"]:
+            r["speedup"] = round(r["triton_us"] / r["ours_us"], 3)
+        if mine.get("full_call_us") and r.get("full_call_us"):
+            r["full_call_speedup"] = round(r["full_call_us"] / mine["full_call_us"], 3)
+        diffs = []
+        for key, arr in ours.items():
+            if key.startswith(f + "_") and key in theirs:
+                diffs.append(float(np.max(np.abs(arr.astype(np.float64) - theirs[key]))) if arr.size else 0.0)
+        if diffs:
+            r["max_abs_diff_vs_ours"] = max(diffs)
+    rows, cols = sample_window(cfg)
+    res["compared_window"] = f"outputs [:{rows}, :{cols}] of input set 0"
+    return res
+
+
+# --------------------------------------------------------------------------
+def oracle_output(fname, h, cfg, precision):
+    """The fp32 / fp64 C oracle's outputs of one function on host inputs `h`."""
+    from oracle import oracle as orc
+
+    tr = cfg["trunc"]
+    trunc, boot = (h["trunc"], h["boot"]) if tr else (None, None)
+    if fname == "gae":
+        return (orc.gae(h["r"], h["v"], h["term"], trunc, boot, orc.BOOT_FULL_SEL if tr else orc.BOOT_NONE,
+                        0.99, 0.95, precision),)
+    if fname == "vtrace":
+        return orc.vtrace(h["lpt"], h["lpb"], h["v"], h["r"], h["term"], trunc, boot,
+                          orc.BOOT_FULL_ADD if tr else orc.BOOT_NONE, 0.99, 1.0, 1.0, precision)
+    if fname == "retrace":
+        return orc.retrace(h["pi"], h["mu"], h["q"], h["nq"], h["act"], h["r"], h["term"],
+                           h["trunc"] if tr else h["notrunc"], 0.99, 0.95, 1.0, 1.0, precision)
+    if fname == "lambda":
+        return (orc.lambda_returns(h["r"], h["nv"], h["term"], trunc, boot, orc.BOOT_FULL_ADD if tr else orc.BOOT_NONE,
+                                   0.99, 0.95, precision),)
+    if fname == "discounted":
+        return (orc.discounted_returns(h["r"], h["term"], trunc, boot, orc.BOOT_FULL_ADD if tr else orc.BOOT_NONE,
+                                       0.99, precision),)
+    if fname == "eligibility":
+        return (orc.eligibility_traces(h["r"], h["term"], 0.99, 0.95, precision=precision),)
+    return (orc.prefix_sum(h["r"], h["term"], precision=precision),)
+
+
+def check_parity(cfg, x, calls, split, world, rank):
+    """After the timed region: every output of input set 0 (all ranks' segments
+    gathered when the sequence is split along time) against the fp32 C oracle
+    at rtol = atol = 1e-5 (oracle.compare)."""
+    from oracle import oracle as orc
+
+    outs = {}
+    for f, c in calls.items():
+        outs.update({k: v for k, v in flat_outputs(f, c()).items()})
+    torch.cuda.synchronize()
+    xs = {k: v for k, v in x.items() if _used(k, cfg) or k == "notrunc"}
+    if split:
+        import torch.distributed as dist
+
+        def gather(t):
+            t = t.contiguous().view(-1)
+            full = torch.empty(world * t.numel(), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(full, t)
+            return full.view(1, -1)
+
+        xs = {k: gather(v) for k, v in xs.items()}
+        outs = {k: gather(v) for k, v in outs.items()}
+        cfg = dict(cfg, T=cfg["T"] * world)
+    if rank != 0:
+        return None
+    h = to_numpy(xs)
+    per = {}
+    for f in cfg["funcs"]:
+        for k in range(2 if f in ("vtrace", "retrace") else 1):
+            key = f"{f}_{k}"
+            got = outs[key].cpu().numpy()
+            res = orc.compare(got, lambda p: oracle_output(f, h, cfg, p)[k])
+            per[key] = {kk: (round(v, 9) if isinstance(v, float) else v) for kk, v in res.items()
+                        if kk not in ("rtol", "atol")}
+    return {"ok": all(r["ok"] for r in per.values()), "max_abs_err": max(r["max_abs_err"] for r in per.values()),
+            "rtol": 1e-5, "atol": 1e-5,
+            "checked": f"every output of input set 0 ({cfg['N']}x{cfg['T']}) against the fp32 C oracle",
+            "per_output": per}
+
+
+# --------------------------------------------------------------------------
+def run_e2e(cfg, x0, dev, split, world, ksteps):
+    """The same step through the public API from pinned host buffers: every step
+    copies its inputs host->device and its outputs device->host.  Copies in,
+    the calls and copies out run on three streams with two buffer sets, so step
+    k+1's inputs travel while step k computes and step k-1's results return."""
+    keys = [k for k in x0 if _used(k, cfg)]
+    host = {k: x0[k].to("cpu").pin_memory() for k in keys}
+    const = {k: v for k, v in x0.items() if k == "notrunc"}  # device constant, not per-step data
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    bufs = [{k: torch.empty_like(x0[k]) for k in keys} for _ in range(2)]
+    cs, ks, ds = (torch.cuda.Stream(dev) for _ in range(3))
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
+    pinned = [None, None]
+
+    def step(k):
+        b = k % 2
+        with torch.cuda.stream(cs):
+            if k >= 2:
+                cs.wait_event(ev_free[b])  # step k-2 finished reading this buffer set
+            for key in keys:
+                bufs[b][key].copy_(host[key], non_blocking=True)
+            ev_in[b].record(cs)
+        with torch.cuda.stream(ks):
+            ks.wait_event(ev_in[b])
+            res = []
+            for f, c in make_calls(cfg, {**bufs[b], **const}, split).items():
+                res.extend(flat_outputs(f, c()).values())
+            ev_free[b].record(ks)
+        with torch.cuda.stream(ds):
+            ds.wait_event(ev_free[b])
+            if pinned[b] is None:
+                pinned[b] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+            for o, r in zip(pinned[b], res):
+                o.copy_(r, non_blocking=True)
+                r.record_stream(ds)
+        return res
+
+    for k in range(4):  # warm-up, allocates the pinned result buffers
+        step(k)
+    torch.cuda.synchronize(dev)
+    d2h = sum(o.numel() * o.element_size() for o in pinned[0])
+    barrier(world)
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a0.record(cs)
+    ks.wait_stream(cs)
+    ds.wait_stream(cs)
+    for k in range(ksteps):
+        step(k)
+    a1.record(ds)
+    torch.cuda.synchronize(dev)
+    ms = max_over_ranks(a0.elapsed_time(a1) / ksteps, world)
+    return {"value": world * cfg["N"] * cfg["T"] / (ms / 1e3), "unit": "timesteps/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "path": "rl_triton public API; pinned host buffers; per step H2D of every input, the calls, D2H of "
+                    "every output; copies in / calls / copies out on three streams, two buffer sets"}
 
 
 def run_b200(args, world, rank, local):
@@ -382,8 +712,7 @@ def run_b200(args, world, rank, local):
     from rl_triton import _native as nat
 
     N, T = cfg["N"], cfg["T"]
-    per_set = sum(bytes_per_step(f, cfg["trunc"], cfg["bf16"]) for f in cfg["funcs"]) * N * T
-    n_sets = max(1, min(8, int(np.ceil(3 * 126e6 / per_set)))) if per_set < 3 * 126e6 else 1
+    n_sets, per_set = input_sets(cfg)
     if args.sets:
         n_sets = args.sets
     sets = [make_inputs(cfg, dev, seed=1000 * rank + k) for k in range(n_sets)]
@@ -397,7 +726,7 @@ def run_b200(args, world, rank, local):
                 f()
     stream.synchronize()
 
-    use_graph = not args.no_graph and not split  # the time split reads lengths on the host
+    use_graph = not args.no_graph and not split  # the split path's collectives run eagerly
     graphs = []
     if use_graph:
         for c in calls:
@@ -431,88 +760,47 @@ def run_b200(args, world, rank, local):
         ev1.record(stream)
     stream.synchronize()
     tw1 = time.perf_counter()
+    sampler.stop()
+    clocks = sampler.summary(tw0, tw1)
     barrier(world)
     torch.cuda.synchronize(dev)
     ms_total = ev0.elapsed_time(ev1)
     ms_total = max_over_ranks(ms_total, world)
     ms = ms_total / args.steps
     value = world * N * T / (ms / 1e3)
+    graphs.clear()
 
-    # Per-kernel durations (CUDA events on the launching stream; graph of K launches).
+    # Per-function device time per launch and eager full-call time.
     per_fn = {}
     hbm, peak_kind = peaks()
-    reps = max(8, min(200, args.steps))
     for fname in cfg["funcs"]:
-        g = None
-        if use_graph:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                for k in range(reps):
-                    calls[k % n_sets][fname]()
-        with torch.cuda.stream(stream):
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            if g is not None:
-                g.replay()
-                e0.record(stream)
-                g.replay()
-            else:
-                for k in range(reps):
-                    calls[k % n_sets][fname]()
-                e0.record(stream)
-                for k in range(reps):
-                    calls[k % n_sets][fname]()
-            e1.record(stream)
-        stream.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / reps
+        t = time_function(calls, fname, stream, use_graph, fixed_reps=8 if world > 1 else 0)
+        us = t["us_per_launch"]
         alg = bytes_per_step(fname, cfg["trunc"], cfg["bf16"]) * N * T
-        per_fn[fname] = {"us_per_launch": round(us, 3), "algorithmic_bytes": alg,
+        per_fn[fname] = {"us_per_launch": us, "full_call_us": t["full_call_us"], "algorithmic_bytes": alg,
                          "achieved_gbs": round(alg / (us * 1e-6) / 1e9, 1),
                          "frac": round(alg / (us * 1e-6) / 1e9 / hbm, 4)}
-        del g
-    sampler.stop()
-    clocks = sampler.summary(tw0, tw1)
     dom = max(per_fn, key=lambda f: per_fn[f]["us_per_launch"])
     d = per_fn[dom]
     traffic = read_traffic(dom, args.config)
 
-    # End to end through the public API: pinned host inputs -> device -> 7 calls -> host outputs.
+    # Parity of the timed path's outputs.
+    parity = None if args.no_parity else check_parity(cfg, sets[0], calls[0], split, world, rank)
+
+    # The reference's own Triton kernels on this GPU (child process).
+    tri = None
+    if rank == 0 and world == 1 and not args.no_triton:
+        rows, cols = sample_window(cfg)
+        ours = {}
+        with torch.cuda.stream(stream):
+            for f, c in calls[0].items():
+                for key, t in flat_outputs(f, c()).items():
+                    ours[key] = t[:rows, :cols].float().cpu().numpy()
+        tri = triton_reference(args, cfg, ours, per_fn, local)
+
     e2e = None
     if not args.no_e2e:
-        host = {k: v.to("cpu").pin_memory() for k, v in sets[0].items()}
-        h2d = sum(v.numel() * v.element_size() for k, v in host.items() if _used(k, cfg))
-        outs_bytes = []
-        pinned_out = []  # results land in pinned host buffers (allocated on the first step)
-
-        def e2e_step():
-            xd = {k: v.to(dev, non_blocking=True) for k, v in host.items() if _used(k, cfg)}
-            res = []
-            for f in make_calls(cfg, xd, split).values():
-                r = f()
-                res.extend(r if isinstance(r, tuple) else (r,))
-            if not pinned_out:
-                pinned_out.extend(torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res)
-                outs_bytes.append(sum(o.numel() * o.element_size() for o in pinned_out))
-            for o, r in zip(pinned_out, res):
-                o.copy_(r, non_blocking=True)
-            return pinned_out
-
-        with torch.cuda.stream(stream):
-            for _ in range(2):
-                e2e_step()
-        stream.synchronize()
-        ksteps = max(3, min(args.steps, 20))
-        barrier(world)
-        with torch.cuda.stream(stream):
-            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a0.record(stream)
-            for _ in range(ksteps):
-                e2e_step()
-            a1.record(stream)
-        stream.synchronize()
-        ms_e2e = max_over_ranks(a0.elapsed_time(a1) / ksteps, world)
-        e2e = {"value": world * N * T / (ms_e2e / 1e3), "unit": "timesteps/s", "ms_per_step": ms_e2e,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(outs_bytes[0]),
-               "path": "rl_triton public API, pinned host buffers, H2D + 7 calls + D2H per step"}
+        e2e = run_e2e(cfg, sets[0], dev, split, world, max(3, min(args.steps, 20)))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -529,17 +817,15 @@ def run_b200(args, world, rank, local):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong" if split else "weak", "vs_baseline": None,
             "dtype": "bf16->f32" if cfg["bf16"] else "f32",
-            "data": "synthetic (seeded torch.Generator; BASELINE config distributions)",
-            "config": {"workload": cfg["desc"], "functions": cfg["funcs"], "num_envs_per_gpu": N,
-                       "seq_len": T, "parallelism": (f"time-split x{world}" if split else f"env-sharded x{world}") if world > 1
-                       else "single GPU",
-                       "l2": f"{n_sets} rotating input sets ({per_set * n_sets / 1e6:.0f} MB > 126 MB L2)",
-                       "launch": "CUDA graph per input set" if use_graph else "eager"},
+            "data": "synthetic (seeded torch.Generator; distributions of the headline configurations)",
+            "config": config_dict(cfg, world, split, n_sets, per_set, use_graph),
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": d["achieved_gbs"], "peak": hbm,
                          "unit": "GB/s", "frac": d["frac"], "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s"},
             "per_function": per_fn,
+            "parity": parity,
+            "triton_reference": tri,
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -598,7 +884,7 @@ def _used(key, cfg):
     if cfg["trunc"]:
         need |= {"trunc", "boot", "nv"}
     if "retrace" in fs:
-        need |= {"pi", "act", "mu", "q", "nq", "trunc32", "term32", "r32"}
+        need |= {"pi", "act", "mu", "q", "nq"}
     return key in need
 
 
@@ -619,7 +905,15 @@ def main():
     ap.add_argument("--only", default="", help="comma list of functions to run (default: all of the config)")
     ap.add_argument("--envs", type=int, default=0, help="--ncu mode: override num_envs (a smaller slice to profile)")
     ap.add_argument("--len", type=int, default=0, help="--ncu mode: override the sequence length T")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed outputs")
+    ap.add_argument("--no-triton", action="store_true", help="skip timing the reference's Triton kernels")
+    ap.add_argument("--triton-worker", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--device", type=int, default=0, help=argparse.SUPPRESS)
+    ap.add_argument("--triton-out", default="", help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.triton_worker:
+        triton_worker(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

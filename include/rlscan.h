@@ -5,7 +5,7 @@
  * (simonsays1980/rl-triton v0.1.3).  The reference binds its kernels from
  * Python through Triton's launcher; this library is bound from Python through
  * ctypes (rl_triton/_native.py), and any other host language can bind the same
- * symbols (INTEGRATION.md shows ctypes, cffi and C++ call sites).
+ * symbols through ctypes, cffi or a direct C/C++ link.
  *
  * Conventions shared by all entry points
  * --------------------------------------
@@ -21,6 +21,11 @@
  *    calls (an epoch counter lives inside it).  Calls that share one
  *    workspace must be ordered on one stream.
  *  - `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *  - Before anything is enqueued, every array argument (and the workspace) is
+ *    checked to be device (or managed) memory of ONE GPU; anything else (a
+ *    host pointer, arrays on two GPUs) returns RLS_ENOTDEVICE.  The call runs
+ *    with that GPU current and restores the caller's current device; `stream`
+ *    must belong to that GPU.
  *  - Return value: RLS_OK (0) or an RLS_E* status; rls_status_string() names
  *    it.  Launches are asynchronous; device-side failures (a bounded wait that
  *    ran out) are latched in the workspace and read with rls_workspace_error().
@@ -43,6 +48,7 @@ extern "C" {
 #define RLS_ECUDA         4   /* CUDA launch / runtime error               */
 #define RLS_EUNSUPPORTED  5   /* combination not implemented               */
 #define RLS_ETOOLARGE     6   /* larger than rls_gae_noalloc's fixed scratch */
+#define RLS_ENOTDEVICE    7   /* an array is not device memory of one GPU  */
 
 /* ---- input element types --------------------------------------------- */
 #define RLS_F32   0
@@ -200,15 +206,16 @@ int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtyp
  * No counterpart in the reference (its Triton path always allocates through
  * PyTorch).  Same arguments and results as rls_gae, minus the workspace: the
  * look-back scratch lives in a fixed array inside the library
- * (RLS_NOALLOC_MAX_ELEMENTS elements' worth, about 5 MB, held on every GPU
+ * (RLS_NOALLOC_MAX_ELEMENTS elements' worth, about 6 MB, held on every GPU
  * that loads the library until the process exits).  Meant for callers that
  * must not call cudaMalloc -- code running while a CUDA graph is being
  * captured into a pool they do not own, real-time loops with a frozen memory
  * budget, or hosts that only hand out buffers they allocated themselves.
  *  - num_envs * seq_len above RLS_NOALLOC_MAX_ELEMENTS returns RLS_ETOOLARGE.
- *  - The call allocates nothing; it clears the scratch's counters with two
+ *  - The call allocates nothing; it clears the scratch's counters with one
  *    small cudaMemsetAsync on `stream`, then launches the same kernels as
- *    rls_gae.
+ *    rls_gae.  Bounded device waits that run out latch an error bit in the
+ *    scratch; rls_gae_noalloc_error() reads it.
  *  - The first call on a device looks the array's device address up
  *    (cudaGetSymbolAddress); make that first call before any stream capture.
  *  - Every call shares the one array: calls that may overlap on the GPU (on
@@ -221,6 +228,13 @@ int rls_gae_noalloc(const void* rewards, const void* values, const void* termina
                     float* advantages, int64_t num_envs, int64_t seq_len,
                     float gamma, float lambda_, int in_dtype,
                     const rls_segment_t* seg, void* stream);
+
+/* Error latch of the current device's fixed scratch: synchronises `stream`,
+ * returns 0 when no bounded device wait of rls_gae_noalloc ran out since the
+ * last read (else the bit mask of rls_workspace_error, or -1 if the scratch
+ * cannot be reached) and clears it.  A wait that ran out means that call's
+ * advantages are wrong.                                                      */
+int rls_gae_noalloc_error(void* stream);
 
 #ifdef __cplusplus
 }

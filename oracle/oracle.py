@@ -214,3 +214,35 @@ def affine_scan(u, v, carry=None, direction=0, precision="f32", nthreads=None):
 
     _rows(N, go, nthreads)
     return out
+
+
+def compare(got, oracle, rtol=1e-5, atol=1e-5):
+    """Parity verdict of a result against the oracle.
+
+    `oracle(precision)` returns the oracle's output ("f32" or "f64").  The
+    result passes when it is within rtol / atol of the fp32 sequential oracle
+    (the reference's own fp32 loop order).  Only where the fp32 oracle is itself
+    off the fp64 oracle by more than that tolerance (long running sums, where
+    any reassociation differs by more than 1e-5) does it pass instead when its
+    worst error against fp64 is at most twice the fp32 oracle's plus atol.
+    Returns a dict: ok, max_abs_err (vs fp32 oracle), criterion, and, when the
+    fp64 leg ran, err_vs_f64 and oracle_f32_err_vs_f64."""
+    got = np.asarray(got, dtype=np.float64)
+    w32 = np.asarray(oracle("f32"), dtype=np.float64)
+    diff = np.abs(got - w32)
+    res = {"max_abs_err": float(diff.max()) if diff.size else 0.0, "rtol": rtol, "atol": atol}
+    if not diff.size or bool(np.all(diff <= atol + rtol * np.abs(w32))):
+        res.update(ok=True, criterion="fp32 oracle within rtol/atol")
+        return res
+    w64 = np.asarray(oracle("f64"), dtype=np.float64)
+    ours = float(np.max(np.abs(got - w64)))
+    ref_dev = np.abs(w32 - w64)
+    ref = float(ref_dev.max())
+    ref_outside = bool(np.any(ref_dev > atol + rtol * np.abs(w64)))
+    res.update(err_vs_f64=ours, oracle_f32_err_vs_f64=ref)
+    if ref_outside:
+        res.update(ok=ours <= 2 * ref + atol, criterion="fp32 oracle itself outside tolerance of fp64: "
+                                                        "error vs fp64 <= 2x the fp32 oracle's + atol")
+    else:
+        res.update(ok=False, criterion="fp32 oracle within tolerance of fp64, result is not")
+    return res

@@ -11,6 +11,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <initializer_list>
+
 namespace rls {
 
 // Affine map  c -> a + b*c  (state at the near end as a function of the carry
@@ -185,5 +187,48 @@ __device__ __forceinline__ void store_run(float* p, int64_t i, int64_t M, bool f
 // workspace and the kernel carries on with an identity carry, so a broken
 // invariant shows up as a host-visible status, never as a hung GPU.
 constexpr unsigned kSpinLimit = 1u << 22;  // ~0.3 s with the nanosleep back-off
+
+// ---- host: pointer placement and device guard ------------------------------
+// Every entry point checks, before it enqueues anything, that each non-null
+// array argument is memory of one CUDA device (device or managed memory, not
+// pageable or pinned host memory), and runs the call with that device current,
+// restoring the caller's device afterwards.  A host pointer handed to a kernel
+// would fault the GPU; here it returns a status instead.
+class DeviceGuard {
+ public:
+  // status(): 0 = ok; otherwise RLS_ENOTDEVICE (7) from rlscan.h.
+  DeviceGuard(std::initializer_list<const void*> ptrs) {
+    int dev = -1;
+    for (const void* p : ptrs) {
+      if (!p) continue;
+      cudaPointerAttributes at;
+      if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();  // clear the sticky-free error the query leaves
+        status_ = 7;
+        return;
+      }
+      if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged) { status_ = 7; return; }
+      if (dev < 0) dev = at.device;
+      else if (at.device != dev) { status_ = 7; return; }
+    }
+    if (dev < 0) return;
+    if (cudaGetDevice(&prev_) != cudaSuccess) { cudaGetLastError(); prev_ = -1; }
+    if (prev_ != dev) {
+      if (cudaSetDevice(dev) != cudaSuccess) { status_ = 7; prev_ = -1; return; }
+      switched_ = true;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched_ && prev_ >= 0) cudaSetDevice(prev_);
+  }
+  int status() const { return status_; }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+
+ private:
+  int status_ = 0;
+  int prev_ = -1;
+  bool switched_ = false;
+};
 
 }  // namespace rls

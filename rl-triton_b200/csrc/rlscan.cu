@@ -25,6 +25,37 @@ constexpr int64_t kMinTileElems = 128;  // smallest tile of any launch (a one-ro
 
 inline bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15u) == 0; }
 
+// Two record layouts share one workspace: the flags | aggregates | inclusive
+// layout of the flat look-back and tile kernels (ws_carve), and the packed
+// 64-bit value|tag words of flat2/3/4 (packed_carve).  A stale float left by
+// one layout could carry bits equal to a valid tag of the other, so the first
+// launch of a layout on a workspace last used by the other one clears the
+// records (the header, with the epoch, is kept).  Tracked per workspace
+// pointer on the host, under the launch lock.
+enum : int { kLayoutNone = 0, kLayoutFlags = 1, kLayoutPacked = 2 };
+int prepare_layout(void* ws, size_t wsb, int layout, cudaStream_t s) {
+  static void* last_ws[64] = {nullptr};
+  static int last_layout[64] = {0};
+  static int next_slot = 0;
+  if (!ws || wsb <= 64) return RLS_OK;
+  int slot = -1;
+  for (int i = 0; i < 64; ++i)
+    if (last_ws[i] == ws) { slot = i; break; }
+  if (slot < 0) {  // first sight: a workspace starts zero-filled
+    slot = next_slot;
+    next_slot = (next_slot + 1) % 64;
+    const bool evicted = last_ws[slot] != nullptr;
+    last_ws[slot] = ws;
+    last_layout[slot] = evicted ? kLayoutNone : layout;
+    if (!evicted) return RLS_OK;
+  }
+  if (last_layout[slot] != layout) {
+    if (cudaMemsetAsync(static_cast<char*>(ws) + 64, 0, wsb - 64, s) != cudaSuccess) return RLS_ECUDA;
+    last_layout[slot] = layout;
+  }
+  return RLS_OK;
+}
+
 int env_rounds() {
   static int v = [] {
     const char* s = std::getenv("RLS_ROUNDS");
@@ -59,6 +90,7 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   g.ws_cap = ws ? ws_capacity(ws_bytes) : 0;
   if (g.ws_cap < g.num_tiles) return RLS_EWORKSPACE;
+  if (int st = prepare_layout(ws, ws_bytes, kLayoutFlags, s)) return st;
   const size_t smem = (size_t)g.smem_per_warp * kWarps;
   auto kern = scan_kernel<Alg, kWarps, R>;
   if (smem > 0) {
@@ -160,6 +192,7 @@ int launch_tile_k(const typename P::Params& p, TileGeom tg, void* ws, size_t ws_
   if (tg.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   tg.ws_cap = ws ? ws_capacity(ws_bytes) : 0;
   if (tg.ws_cap < tg.num_tiles) return RLS_EWORKSPACE;
+  if (int st = prepare_layout(ws, ws_bytes, kLayoutFlags, s)) return st;
   const size_t smem = (size_t)tg.stages * tg.stage_bytes + (size_t)TILE * 4 * (P::kOutSlots + P::kScratch);
   auto kern = tile_kernel<P, K>;
   int dev = 0;
@@ -277,6 +310,7 @@ int launch_flat2(const typename P::Params& p, const Geom& g0, void* ws, size_t w
   if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
   // Same convention as the other look-back kernels: a launch uses the current
   // epoch and leaves the next one for the following launch on this workspace.
+  if (int st = prepare_layout(ws, wsb, kLayoutPacked, s)) return st;
   flat2_kernel<P, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
   advance_epoch<<<1, 1, 0, s>>>(ws);
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
@@ -291,6 +325,7 @@ int launch_flat3(const typename P::Params& p, const Geom& g0, void* ws, size_t w
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   g.ws_cap = ws ? packed_capacity(wsb) : 0;
   if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
+  if (int st = prepare_layout(ws, wsb, kLayoutPacked, s)) return st;
   g.l2_prefetch = 0;  // the bulk L2 prefetch measured within noise; kept off
   flat3_kernel<P, NCH, R><<<(unsigned)((g.num_tiles + 3) / 4), 128, 0, s>>>(p, g, ws);
   advance_epoch<<<1, 1, 0, s>>>(ws);
@@ -323,6 +358,7 @@ int launch_flat4(const typename P::Params& p, const Geom& g0, void* ws, size_t w
   if (g.num_tiles > 0x3fffffffLL) return RLS_EINVAL;
   g.ws_cap = ws ? packed_capacity(wsb) : 0;
   if (g.ws_cap < g.num_tiles) return launch_tile<P, kTileK>(p, g0, ws, wsb, s);
+  if (int st = prepare_layout(ws, wsb, kLayoutPacked, s)) return st;
   g.l2_prefetch = 0;
   static bool attr = false;  // per instantiation; racing first calls set the same value
   if (!attr) {
@@ -424,15 +460,24 @@ int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t ws
     // per SM from its register count x the SMs), or as many as the workspace
     // holds (four words each).  A partial second wave would leave most SMs idle
     // at the end.
-    static int64_t wave = 0;  // per instantiation; racing first calls compute the same value
+    const VrowsSpec v = VSpec<P>::get(p);
+    // The bounded fix-up assumes the decay product stays within [0, 1] and
+    // only shrinks: other coefficients take flat3.
+    if (!(v.coef > 0.f && v.coef <= 1.f)) return Flat3L<P>::run(p, g, ws, wsb, s);
+    // Per instantiation and device (devices may differ in SM count); racing
+    // first calls compute the same value.
+    static int64_t wave_of[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
+    int64_t wave = dev >= 0 && dev < 64 ? wave_of[dev] : 0;
     if (wave == 0) {
-      int nb = 0, dev = 0, sms = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, vseg_kernel<P>, 128, 0) != cudaSuccess ||
-          cudaGetDevice(&dev) != cudaSuccess ||
-          cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || nb < 1 || sms < 1)
+      int nb = 0;
+      const int sms = num_sms(dev);
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, vseg_kernel<P>, 128, 0) != cudaSuccess || nb < 1)
         wave = kVrowsSegs;
       else
         wave = std::min<int64_t>((int64_t)nb * 4 * sms, 6144);  // vrows_carry stages <= 6144 maps
+      if (dev >= 0 && dev < 64) wave_of[dev] = wave;
     }
     const int64_t room = ws && wsb > 64 ? (int64_t)((wsb - 64) / 16) : 0;
     const int64_t want = room < wave ? room : wave;
@@ -442,7 +487,6 @@ int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t ws
     const int64_t nseg = (g.M + L - 1) / L;
     // auto: the fix-up reaches up to -110 / ln(coef) steps into a segment (the
     // decay product underflows there); keep that under a quarter of it.
-    const VrowsSpec v = VSpec<P>::get(p);
     int64_t min_len = kVrowsMinLen;
     if (v.coef > 0.f && v.coef < 1.f) min_len = std::max(min_len, (int64_t)(4.0 * -110.0 / std::log((double)v.coef)));
     if ((!forced && L < min_len) || L > 0x7fffffffLL) return Flat3L<P>::run(p, g, ws, wsb, s);
@@ -579,6 +623,10 @@ std::recursive_mutex& launch_mutex() {
 
 bool valid_dtype(int d) { return d == RLS_F32 || d == RLS_BF16; }
 
+#define RLS_DEVICE_GUARD(...)              \
+  DeviceGuard device_guard_{__VA_ARGS__};  \
+  if (device_guard_.status()) return device_guard_.status();
+
 }  // namespace
 
 extern "C" {
@@ -619,6 +667,7 @@ const char* rls_status_string(int status) {
       return buf;
     }
     case RLS_EUNSUPPORTED: return "unsupported argument combination";
+    case RLS_ENOTDEVICE: return "an array argument is not device memory of one GPU (host pointer, or arrays on different GPUs)";
     case RLS_ETOOLARGE: return "num_envs * seq_len exceeds RLS_NOALLOC_MAX_ELEMENTS (the fixed scratch of rls_gae_noalloc)";
     default: return "unknown status";
   }
@@ -642,6 +691,7 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
   if (!aligned16(rewards) || !aligned16(values) || !aligned16(terminateds) || !aligned16(truncateds) ||
       !aligned16(advantages) || (boot_kind >= RLS_BOOT_LASTCOL && !aligned16(bootstrap)))
     return RLS_EALIGN;
+  RLS_DEVICE_GUARD(rewards, values, terminateds, truncateds, bootstrap, advantages, seg ? seg->halo : nullptr, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, seg, true, g);
   if (st) return st;
@@ -698,6 +748,8 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
       !aligned16(terminateds) || !aligned16(truncateds) || !aligned16(targets) || !aligned16(advantages) ||
       (boot_kind >= RLS_BOOT_LASTCOL && !aligned16(bootstrap)))
     return RLS_EALIGN;
+  RLS_DEVICE_GUARD(log_pi_target, log_pi_behavior, values, rewards, terminateds, truncateds, bootstrap, targets,
+                   advantages, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, nullptr, true, g);
   if (st) return st;
@@ -752,6 +804,8 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
       !aligned16(next_q_values_all) || !aligned16(actions) || !aligned16(rewards) || !aligned16(terminateds) ||
       !aligned16(truncateds) || !aligned16(targets) || !aligned16(advantages))
     return RLS_EALIGN;
+  RLS_DEVICE_GUARD(action_probs_target, action_probs_behavior, q_values, next_q_values_all, actions, rewards,
+                   terminateds, truncateds, targets, advantages, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, nullptr, true, g);
   if (st) return st;
@@ -802,6 +856,7 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
   if (!aligned16(rewards) || !aligned16(next_values) || !aligned16(terminateds) || !aligned16(truncateds) ||
       !aligned16(bootstrap) || !aligned16(out))
     return RLS_EALIGN;
+  RLS_DEVICE_GUARD(rewards, next_values, terminateds, truncateds, bootstrap, out, seg ? seg->halo : nullptr, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, seg, true, g);
   if (st) return st;
@@ -852,6 +907,7 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
   if (!aligned16(rewards) || !aligned16(terminateds) || !aligned16(truncateds) || !aligned16(bootstrap) ||
       !aligned16(out))
     return RLS_EALIGN;
+  RLS_DEVICE_GUARD(rewards, terminateds, truncateds, bootstrap, out, seg ? seg->halo : nullptr, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, seg, true, g);
   if (st) return st;
@@ -896,6 +952,7 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
   if (!x || !dones || !out || !valid_dtype(in_dtype)) return RLS_EINVAL;
   if (seg && prev && seg->t0 > 0 && !seg->halo) return RLS_EINVAL;
   if (!aligned16(x) || !aligned16(dones) || !aligned16(out)) return RLS_EALIGN;
+  RLS_DEVICE_GUARD(x, dones, seed, out, seg ? seg->halo : nullptr, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, seg, false, g);
   if (st) return st;
@@ -953,6 +1010,7 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
   if (num_envs == 0 || seq_len == 0) return (num_envs < 0 || seq_len < 0) ? RLS_EINVAL : RLS_OK;
   if (!u || !v || !out || (direction != 0 && direction != 1)) return RLS_EINVAL;
   if (!aligned16(u) || !aligned16(v) || !aligned16(out)) return RLS_EALIGN;
+  RLS_DEVICE_GUARD(u, v, carry, out, seg ? seg->halo : nullptr, ws)
   Geom g;
   int st = make_geom(num_envs, seq_len, seg, direction == 0, g);
   if (st) return st;
@@ -988,22 +1046,48 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
 
 // ---------------------------------------------------------------------------
 // rls_gae_noalloc: GAE whose look-back scratch is a fixed array in this file,
-// for callers that cannot allocate device memory.  The array is sized for the
-// smallest tiles any GAE launch uses (kMinTileElems elements), so every path
-// (tile, row, flat) fits up to RLS_NOALLOC_MAX_ELEMENTS elements.  It starts
-// zero-filled, as the look-back protocol requires; the kernels keep it
-// consistent from call to call (epoch-tagged flags), and each call clears the
-// ticket / exit counters and the error latch before launching.
+// for callers that cannot allocate device memory.  Every GAE launch family
+// uses tiles of at least kNoAllocMinTile elements (the flat look-back kernel:
+// 4 warps x 32 lanes x one fp32 vector; flat2: 32 lanes x 4 rounds x 4; the
+// tile kernel, flat3 and the row kernels use larger tiles or none), so
+// RLS_NOALLOC_MAX_ELEMENTS / kNoAllocMinTile tile records in the larger of the
+// two record layouts (24 bytes per tile, flat2's packed words) cover every path
+// up to the maximum size.  The array starts zero-filled, as the look-back
+// protocol requires; the kernels keep it consistent from call to call
+// (epoch-tagged flags), and each call clears the ticket and exit counters
+// before launching.  The error latch is left alone: rls_gae_noalloc_error()
+// reads and clears it.
 namespace {
-constexpr int64_t kNoAllocTiles = RLS_NOALLOC_MAX_ELEMENTS / 512;  // 512-step tiles (tile, flat kernels)
-constexpr size_t kNoAllocBytes = 64 + (size_t)kNoAllocTiles * 4 + (size_t)kNoAllocTiles * 16;
-static_assert(kNoAllocTiles * 4 % 16 == 0, "flag array keeps the aggregate array 16-byte aligned");
+constexpr int64_t kNoAllocMinTile = 512;
+static_assert((int64_t)kWarps * 32 * InTraits<float>::kVec >= kNoAllocMinTile,
+              "flat look-back tiles are at least kNoAllocMinTile elements");
+static_assert(32LL * 4 * (16 / (int)sizeof(float)) >= kNoAllocMinTile, "flat2 tiles are at least kNoAllocMinTile");
+static_assert((int64_t)kTileThreads * kTileK >= kNoAllocMinTile, "tile-kernel tiles are at least kNoAllocMinTile");
+constexpr int64_t kNoAllocTiles = RLS_NOALLOC_MAX_ELEMENTS / kNoAllocMinTile;
+constexpr size_t kNoAllocBytes = 64 + (size_t)kNoAllocTiles * 24;
+static_assert(kNoAllocBytes >= 64 + (size_t)kNoAllocTiles * 20 + 16, "room for the flags layout too");
 
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {nullptr};
 }  // namespace
 
 static __device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocBytes];
+
+// Device address of this GPU's copy of the scratch (looked up once per device,
+// with that device current).
+static void* noalloc_scratch(int* status) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) { *status = RLS_ECUDA; return nullptr; }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    // The host-side name of the array is not a device address.
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_ws) != cudaSuccess || !p) { *status = RLS_ECUDA; return nullptr; }
+    g_noalloc_ptr[dev] = p;
+  }
+  *status = RLS_OK;
+  return g_noalloc_ptr[dev];
+}
 
 extern "C" int rls_gae_noalloc(const void* rewards, const void* values, const void* terminateds,
                                const void* truncateds, const void* bootstrap, int boot_kind, float* advantages,
@@ -1012,26 +1096,24 @@ extern "C" int rls_gae_noalloc(const void* rewards, const void* values, const vo
   if (num_envs < 0 || seq_len < 0) return RLS_EINVAL;
   if (num_envs == 0 || seq_len == 0) return RLS_OK;
   if (num_envs > RLS_NOALLOC_MAX_ELEMENTS / seq_len) return RLS_ETOOLARGE;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return RLS_ECUDA;
-  void* ws = nullptr;
-  {
-    // Set-up, once per device with that device current: the host-side name of
-    // the array is not a device address, so look the address up.
-    std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_ptr[dev]) {
-      void* p = nullptr;
-      if (cudaGetSymbolAddress(&p, g_noalloc_ws) != cudaSuccess || !p) return RLS_ECUDA;
-      g_noalloc_ptr[dev] = p;
-    }
-    ws = g_noalloc_ptr[dev];
-  }
+  if (!rewards || !values || !terminateds || !advantages) return RLS_EINVAL;
+  // The scratch used is the copy on the GPU that holds the arrays.
+  RLS_DEVICE_GUARD(rewards, values, terminateds, truncateds, bootstrap, advantages, seg ? seg->halo : nullptr)
+  int st = RLS_OK;
+  void* ws = noalloc_scratch(&st);
+  if (!ws) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
-  // Ticket and exit counters (bytes 0-7) and the error latch (12-15); the
-  // epoch (8-11) must keep counting up.
+  // Ticket and exit counters (bytes 0-7); the epoch (8-11) must keep counting
+  // up and the error latch (12-15) keeps its bits until it is read.
   if (cudaMemsetAsync(ws, 0, 8, s) != cudaSuccess) return RLS_ECUDA;
-  if (cudaMemsetAsync((char*)ws + 12, 0, 4, s) != cudaSuccess) return RLS_ECUDA;
   return rls_gae(rewards, values, terminateds, truncateds, bootstrap, boot_kind, advantages, num_envs, seq_len,
                  gamma, lambda_, in_dtype, seg, ws, kNoAllocBytes, stream);
+}
+
+extern "C" int rls_gae_noalloc_error(void* stream) {
+  int st = RLS_OK;
+  void* ws = noalloc_scratch(&st);
+  if (!ws) return -1;
+  return rls_workspace_error(ws, stream);
 }

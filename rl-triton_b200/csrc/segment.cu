@@ -316,8 +316,13 @@ __global__ void __launch_bounds__(kBlockWalk) vrows_fixup(const SegArgs a, int64
     int64_t n = code >= 0 ? (a.backward ? len - 1 - code : code) : len;  // steps that take the carry
     const bool unit = a.coef == 1.f;
     if (!unit) {
-      const float lim = a.coef > 0.f && a.coef < 1.f ? -110.f / logf(a.coef) + 64.f : 0.f;
-      if ((float)n > lim) n = (int64_t)lim;
+      // |coef| < 1: the product underflows to 0 within -110 / ln|coef| steps;
+      // otherwise it never does and every step up to the first reset takes it.
+      const float ac = fabsf(a.coef);
+      if (ac > 0.f && ac < 1.f) {
+        const float lim = -110.f / logf(ac) + 64.f;
+        if ((float)n > lim) n = (int64_t)lim;
+      }
     }
     for (int64_t k0 = 0; k0 < n; k0 += (int64_t)kBlockWalk * kFixBatch) {
       float v[kFixBatch];
@@ -416,6 +421,8 @@ int rls_segment_reduce(int alg, const void* flag0, const void* flag1, int in_dty
   int st = fill_args(alg, flag0, flag1, in_dtype, num_envs, seq_len, coef, flags, seg, a);
   if (st) return st;
   if (!out || !seg_a || !seg_b) return RLS_EINVAL;
+  DeviceGuard guard{flag0, flag1, out, seg_a, seg_b, seg ? seg->halo : nullptr};
+  if (guard.status()) return guard.status();
   a.out = const_cast<float*>(out);
   a.carry = nullptr;
   a.seg_a = seg_a;
@@ -431,6 +438,8 @@ int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtyp
   int st = fill_args(alg, flag0, flag1, in_dtype, num_envs, seq_len, coef, flags, seg, a);
   if (st) return st;
   if (!out || !carry) return RLS_EINVAL;
+  DeviceGuard guard{flag0, flag1, out, carry, seg ? seg->halo : nullptr};
+  if (guard.status()) return guard.status();
   a.out = out;
   a.carry = carry;
   a.seg_a = nullptr;

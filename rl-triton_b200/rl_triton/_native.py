@@ -19,6 +19,7 @@ RLS_OK = 0
 RLS_F32 = 0
 RLS_BF16 = 1
 RLS_ETOOLARGE = 6
+RLS_ENOTDEVICE = 7
 NOALLOC_MAX_ELEMENTS = 1 << 27
 
 BOOT_NONE = 0
@@ -76,6 +77,7 @@ _SIGS = {
     "rls_segment_reduce": (_I, [_I, _P, _P, _I, _P, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
     "rls_segment_fixup": (_I, [_I, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
     "rls_gae_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _F, _F, _I, _SEG, _P]),
+    "rls_gae_noalloc_error": (_I, [_P]),
 }
 for _name, (_res, _args) in _SIGS.items():
     _fn = getattr(lib, _name)
@@ -85,10 +87,15 @@ for _name, (_res, _args) in _SIGS.items():
 EXPORTED = tuple(_SIGS)
 
 
-def check(status: int, what: str) -> None:
+def check(status: int, what: str, device: torch.device | None = None) -> None:
+    """Raise RuntimeError for a non-OK status.  With
+    RL_TRITON_CORRECTNESS_WARNINGS=1 also wait for the call and raise if one
+    of its bounded device waits ran out (see raise_if_device_error)."""
     if status != RLS_OK:
         msg = lib.rls_status_string(status).decode()
         raise RuntimeError(f"{what}: librlscan status {status} ({msg})")
+    if device is not None and os.environ.get("RL_TRITON_CORRECTNESS_WARNINGS", "0") == "1":
+        raise_if_device_error(device)
 
 
 def ptr(t: torch.Tensor | None) -> int | None:
@@ -140,6 +147,18 @@ def workspace_error(device: torch.device | None = None) -> int:
     if buf is None:
         return 0
     return int(lib.rls_workspace_error(ctypes.c_void_p(buf.data_ptr()), ctypes.c_void_p(s)))
+
+
+def raise_if_device_error(device: torch.device | None = None) -> None:
+    """Raise RuntimeError if a bounded device wait ran out on the current
+    stream's workspace since the last read (synchronises the stream).  The
+    estimators call it after every launch when RL_TRITON_CORRECTNESS_WARNINGS=1;
+    otherwise callers may call it when they choose."""
+    err = workspace_error(device)
+    if err:
+        raise RuntimeError(
+            f"librlscan: a bounded device wait ran out (error bits {err:#x}); the results of the calls on this "
+            "stream since the last check are not valid")
 
 
 def build_info() -> str:

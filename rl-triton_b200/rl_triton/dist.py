@@ -133,17 +133,20 @@ def _run(alg, x: dict, p: dict, ref: torch.Tensor, group=None, all_gather=None, 
         edge = x["dones"][:, -1].float()           # our last flag: the next rank's halo
     else:
         edge = torch.zeros(n, dtype=torch.float32, device=dev)
-    meta = torch.cat([torch.full((1,), float(s), dtype=torch.float32, device=dev), edge])
+    # The length travels as two fp32 words (s // 2^20, s % 2^20), each exact
+    # below 2^24, so any length up to 2^44 arrives unrounded.
+    hi, lo = divmod(int(s), 1 << 20)
+    meta = torch.cat([torch.tensor([float(hi), float(lo)], dtype=torch.float32, device=dev), edge])
     metas = all_gather(meta)
     if t0 is None or total is None:  # learn the layout (reads the lengths on the host)
-        lengths = [int(m[0].item()) for m in metas]
+        lengths = [int(m[0].item()) * (1 << 20) + int(m[1].item()) for m in metas]
         t0, total = sum(lengths[:rank]), sum(lengths)
     seg = Segment(rank, world, t0, s, total)
     halo = None
     if alg == GAE and rank + 1 < world:
-        halo = metas[rank + 1][1:].contiguous()
+        halo = metas[rank + 1][2:].contiguous()
     elif alg in (ELIGIBILITY, PREFIX) and rank > 0:
-        halo = metas[rank - 1][1:].contiguous()
+        halo = metas[rank - 1][2:].contiguous()
 
     # (2)-(3) local scan with a cut, then the segment's map.
     out = kernels.scan(alg, x, seg, halo, p)

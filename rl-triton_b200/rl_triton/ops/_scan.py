@@ -87,8 +87,17 @@ def _scalar_f32(t: torch.Tensor | None) -> torch.Tensor | None:
     return _ready(t)
 
 
-def _launch_ctx(ref: torch.Tensor) -> tuple[torch.device, int]:
+def _launch_ctx(ref: torch.Tensor, *others: torch.Tensor | None) -> tuple[torch.device, int]:
+    """Device and current stream of a call, after the always-on placement
+    check: every tensor the kernel reads or writes is a CUDA tensor on the
+    same device as `ref` (the library checks the pointers again and returns
+    RLS_ENOTDEVICE before launching anything)."""
+    assert ref.is_cuda, "inputs must be on CUDA"
     dev = ref.device
+    for t in others:
+        if t is not None:
+            assert t.is_cuda and t.device == dev, \
+                f"all tensors of one call must be on {dev}; got a tensor on {t.device}"
     return dev, nat.stream_handle(dev)
 
 
@@ -117,9 +126,9 @@ def _run_scan(
     if not v.is_contiguous():
         _perf_warn("v is not contiguous; a copy will be made. Call .contiguous() before the hot loop to avoid this overhead.")
 
+    assert u.is_cuda and v.is_cuda, "u and v must be on CUDA"  # always on: a host pointer never reaches a kernel
     if _CORRECTNESS_WARNINGS():
         assert u.shape == v.shape,      "u and v must have the same shape"
-        assert u.is_cuda and v.is_cuda, "u and v must be on CUDA"
         assert u.dtype == torch.float32, f"u: expected float32, got {u.dtype}"
         assert v.dtype == torch.float32, f"v: expected float32, got {v.dtype}"
         if bootstrap is not None:
@@ -146,9 +155,9 @@ def _run_scan_forward(
     if not v.is_contiguous():
         _perf_warn("v is not contiguous; a copy will be made. Call .contiguous() before the hot loop to avoid this overhead.")
 
+    assert u.is_cuda and v.is_cuda, "u and v must be on CUDA"  # always on: a host pointer never reaches a kernel
     if _CORRECTNESS_WARNINGS():
         assert u.shape == v.shape,      "u and v must have the same shape"
-        assert u.is_cuda and v.is_cuda, "u and v must be on CUDA"
         assert u.dtype == torch.float32, f"u: expected float32, got {u.dtype}"
         assert v.dtype == torch.float32, f"v: expected float32, got {v.dtype}"
         if seed is not None:
@@ -165,11 +174,11 @@ def _affine(u, v, carry, direction, segment=None, out=None):
     num_envs, seq_len = u.shape
     if out is None:
         out = torch.empty_like(u)
-    dev, s = _launch_ctx(u)
+    dev, s = _launch_ctx(u, v, carry, out)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_affine_scan(
         u.data_ptr(), v.data_ptr(), nat.ptr(carry), direction, out.data_ptr(),
         num_envs, seq_len, segment, ws, wsb, s,
     )
-    nat.check(st, "rls_affine_scan")
+    nat.check(st, "rls_affine_scan", dev)
     return out

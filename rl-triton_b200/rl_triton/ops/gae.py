@@ -117,12 +117,12 @@ def compute_gae(
     row = _scalar_f32(last_value)
 
     out = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    dev, s = _launch_ctx(rewards)
+    dev, s = _launch_ctx(rewards, values, terminateds, truncateds, boot, row, out)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_gae(
         rewards.data_ptr(), values.data_ptr(), terminateds.data_ptr(), nat.ptr(truncateds),
         nat.ptr(row if kind == nat.BOOT_ROW else boot), kind, out.data_ptr(),
         num_envs, seq_len, float(gamma), float(lambda_), dt, _segment, ws, wsb, s,
     )
-    nat.check(st, "rls_gae")
+    nat.check(st, "rls_gae", dev)
     return out

@@ -38,8 +38,8 @@ def compute_episodic_prefix_sum(
     """
     num_envs, seq_len = inputs.shape
 
+    assert inputs.is_cuda and dones.is_cuda, "inputs and dones must be on CUDA"  # always on
     if _CORRECTNESS_WARNINGS():
-        assert inputs.is_cuda and dones.is_cuda, "inputs and dones must be on CUDA"
         assert inputs.dtype in (torch.float32, torch.bfloat16), f"inputs: expected float32, got {inputs.dtype}"
         assert dones.dtype in (torch.float32, torch.bfloat16),  f"dones: expected float32, got {dones.dtype}"
         assert inputs.shape == dones.shape,   "inputs and dones must have the same shape"
@@ -58,11 +58,11 @@ def compute_episodic_prefix_sum(
     dones = _ready(dones, "dones")
     seed = _scalar_f32(seed_values)
     out = torch.empty(inputs.shape, dtype=torch.float32, device=inputs.device)
-    dev, s = _launch_ctx(inputs)
+    dev, s = _launch_ctx(inputs, dones, seed, out)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_prefix_sum(
         inputs.data_ptr(), dones.data_ptr(), nat.ptr(seed), ends_at, out.data_ptr(),
         num_envs, seq_len, dt, _segment, ws, wsb, s,
     )
-    nat.check(st, "rls_prefix_sum")
+    nat.check(st, "rls_prefix_sum", dev)
     return out

@@ -28,7 +28,7 @@ def _retrace_launch(action_probs_target, action_probs_behavior, q_values, next_q
     trunc = f(truncateds, "truncateds")
     targets = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
     advantages = torch.empty_like(targets)
-    dev, s = _launch_ctx(rewards)
+    dev, s = _launch_ctx(rewards, pi, mu, q, nq, act, term, trunc, targets, advantages)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_retrace(
         pi.data_ptr(), mu.data_ptr(), q.data_ptr(), nq.data_ptr(), act.data_ptr(), r.data_ptr(),
@@ -36,7 +36,7 @@ def _retrace_launch(action_probs_target, action_probs_behavior, q_values, next_q
         num_envs, seq_len, num_actions, float(gamma), float(lambda_), float(c_bar), float(rho_bar),
         ws, wsb, s,
     )
-    nat.check(st, "rls_retrace")
+    nat.check(st, "rls_retrace", dev)
     return targets, advantages
 
 

@@ -83,14 +83,14 @@ def compute_lambda_returns(
     truncateds = _ready(truncateds, "truncateds")
     boot = _ready(boot, "bootstrap_values")
     out = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    dev, s = _launch_ctx(rewards)
+    dev, s = _launch_ctx(rewards, next_values, terminateds, truncateds, boot, out)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_lambda_returns(
         rewards.data_ptr(), next_values.data_ptr(), terminateds.data_ptr(), nat.ptr(truncateds),
         nat.ptr(boot), kind, out.data_ptr(), num_envs, seq_len, float(gamma), float(lambda_), dt,
         _segment, ws, wsb, s,
     )
-    nat.check(st, "rls_lambda_returns")
+    nat.check(st, "rls_lambda_returns", dev)
     return out
 
 
@@ -129,13 +129,13 @@ def compute_discounted_returns(
     truncateds = _ready(truncateds, "truncateds")
     boot = _ready(boot, "bootstrap_values")
     out = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    dev, s = _launch_ctx(rewards)
+    dev, s = _launch_ctx(rewards, terminateds, truncateds, boot, out)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_discounted_returns(
         rewards.data_ptr(), terminateds.data_ptr(), nat.ptr(truncateds), nat.ptr(boot), kind,
         out.data_ptr(), num_envs, seq_len, float(gamma), dt, _segment, ws, wsb, s,
     )
-    nat.check(st, "rls_discounted_returns")
+    nat.check(st, "rls_discounted_returns", dev)
     return out
 
 
@@ -177,11 +177,11 @@ def compute_eligibility_traces(
     dones = _ready(dones, "dones")
     seed = _scalar_f32(seed_values)
     out = torch.empty(gradients.shape, dtype=torch.float32, device=gradients.device)
-    dev, s = _launch_ctx(gradients)
+    dev, s = _launch_ctx(gradients, dones, seed, out)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_eligibility_traces(
         gradients.data_ptr(), dones.data_ptr(), nat.ptr(seed), out.data_ptr(), num_envs, seq_len,
         float(gamma), float(lambda_), dt, _segment, ws, wsb, s,
     )
-    nat.check(st, "rls_eligibility_traces")
+    nat.check(st, "rls_eligibility_traces", dev)
     return out

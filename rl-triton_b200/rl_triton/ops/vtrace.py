@@ -40,6 +40,12 @@ def compute_vtrace(
     """
     num_envs, seq_len = rewards.shape
     has_truncations = truncateds is not None
+    # Always on, whichever path serves the call: a host tensor never reaches a kernel.
+    for name, t in [("log_pi_target", log_pi_target), ("log_pi_behavior", log_pi_behavior), ("values", values),
+                    ("rewards", rewards), ("terminateds", terminateds), ("truncateds", truncateds),
+                    ("bootstrap_values", bootstrap_values), ("last_value", last_value)]:
+        if t is not None:
+            assert t.is_cuda, f"{name} must be on CUDA"
 
     if _CORRECTNESS_WARNINGS():
         for name, t in [

@@ -50,7 +50,7 @@ def _vtrace_launch(log_pi_target, log_pi_behavior, values, rewards, terminateds,
 
     targets = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
     advantages = torch.empty_like(targets)
-    dev, s = _launch_ctx(rewards)
+    dev, s = _launch_ctx(rewards, lpt, lpb, values, terminateds, truncateds, boot, row, targets, advantages)
     ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
     st = nat.lib.rls_vtrace(
         lpt.data_ptr(), lpb.data_ptr(), values.data_ptr(), rewards.data_ptr(),
@@ -59,7 +59,7 @@ def _vtrace_launch(log_pi_target, log_pi_behavior, values, rewards, terminateds,
         targets.data_ptr(), advantages.data_ptr(), num_envs, seq_len,
         float(gamma), float(rho_bar), float(c_bar), dt, ws, wsb, s,
     )
-    nat.check(st, "rls_vtrace")
+    nat.check(st, "rls_vtrace", dev)
     return targets, advantages
 
 

@@ -57,8 +57,11 @@ def T(x):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("RL_TRITON_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("RL_TRITON_REFERENCE"),
+                    help="checkout of simonsays1980/rl-triton v0.1.3 (or set RL_TRITON_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or RL_TRITON_REFERENCE) is required")
     sys.dont_write_bytecode = True
     sys.path.insert(0, os.path.join(args.reference, "tests"))
     sys.path.insert(0, os.path.join(args.reference, "src"))

@@ -107,7 +107,29 @@ def _gloo_rank(rank, world, port, outdir, mode):
     if mode == "leave" and rank == world - 1:
         os._exit(0)  # this rank leaves between steps, before the exchange
     try:
-        if mode == "leave":
+        if mode == "long":
+            # Segment lengths that fp32 cannot hold exactly (2^24 + 1) still
+            # give each rank its true t0 and the total length.
+            n0, n1 = (1 << 24) + 1, 3
+            x = _inputs(1, n0 + n1, 5)
+            lo, hi = (0, n0) if rank == 0 else (n0, n0 + n1)
+            seen = {}
+
+            class Recording(CpuKernels):
+                def scan(self, alg, xx, seg, halo, p):
+                    seen.update(t0=seg.t0, total=seg.total)
+                    return super().scan(alg, xx, seg, halo, p)
+
+            got = D.compute_episodic_prefix_sum(torch.from_numpy(x["r"][:, lo:hi].copy()),
+                                                torch.from_numpy(x["term"][:, lo:hi].copy()),
+                                                kernels=Recording())
+            assert seen == dict(t0=lo, total=n0 + n1), seen
+            want = orc.prefix_sum(x["r"], x["term"])[:, lo:hi]
+            res = orc.compare(got.numpy(), lambda pr: orc.prefix_sum(x["r"], x["term"], precision=pr)[:, lo:hi])
+            assert res["ok"], res
+            del want
+            np.save(os.path.join(outdir, f"r{rank}.npy"), np.array([1]))
+        elif mode == "leave":
             x = _inputs(2, 50, 0)
             _segment_call("prefix_ends", x, rank, world, lambda t: t, kernels=CpuKernels())
             np.save(os.path.join(outdir, f"r{rank}.npy"), np.array([0]))  # should not get here
@@ -149,6 +171,13 @@ def test_time_split_gloo_matches_whole_sequence(world):
     errs = {k: v for k, v in files.items() if k.endswith(".err")}
     assert not errs, errs
     assert sorted(k for k in files if k.endswith(".npy")) == [f"r{r}.npy" for r in range(world)]
+
+
+def test_time_split_lengths_beyond_fp32_exact_range():
+    files = _spawn(2, "long")
+    errs = {k: v for k, v in files.items() if k.endswith(".err")}
+    assert not errs, errs
+    assert sorted(k for k in files if k.endswith(".npy")) == ["r0.npy", "r1.npy"]
 
 
 def test_time_split_rank_that_leaves_fails_the_others_without_hanging():

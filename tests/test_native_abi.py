@@ -72,3 +72,18 @@ def test_misaligned_pointer_rejected():
     bad = a + 4
     st = nat.lib.rls_discounted_returns(bad, a, None, None, 0, a, 2, 8, 0.99, 0, None, a, 1 << 16, None)
     assert st == 2
+
+
+def test_host_pointers_are_rejected_before_any_launch():
+    """Aligned, non-null host memory: every entry point answers RLS_ENOTDEVICE
+    before it enqueues anything (here there is not even a GPU to enqueue on)."""
+    buf = (ctypes.c_float * 256)()
+    base = ctypes.addressof(buf)
+    a = base + (16 - base % 16) % 16
+    assert nat.lib.rls_gae(a, a, a, None, None, 0, a, 2, 8, 0.99, 0.95, 0, None, a, 512, None) == nat.RLS_ENOTDEVICE
+    assert nat.lib.rls_prefix_sum(a, a, None, 1, a, 2, 8, 0, None, a, 512, None) == nat.RLS_ENOTDEVICE
+    assert nat.lib.rls_affine_scan(a, a, None, 0, a, 2, 8, None, a, 512, None) == nat.RLS_ENOTDEVICE
+    assert nat.lib.rls_vtrace(a, a, a, a, a, None, None, 0, a, a, 2, 8, 0.99, 1.0, 1.0, 0, a, 512,
+                              None) == nat.RLS_ENOTDEVICE
+    assert nat.lib.rls_gae_noalloc(a, a, a, None, None, 0, a, 2, 8, 0.99, 0.95, 0, None, None) == nat.RLS_ENOTDEVICE
+    assert "not device memory" in nat.lib.rls_status_string(nat.RLS_ENOTDEVICE).decode()

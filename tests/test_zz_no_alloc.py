@@ -8,9 +8,12 @@ rls_gae_noalloc serves them: its look-back scratch is a fixed array inside the
 library, so the caller passes only inputs and outputs.
 
 These tests call the entry point through the C ABI (ctypes) and check it
-against rls_gae with a caller-provided workspace, twice in a row (the second
-call reuses the array the first one left behind), at the parity tolerance of
-the other GPU tests.  The file is named so that pytest collects it last.
+against rls_gae with a caller-provided workspace and against the fp32 C
+oracle, twice in a row (the second call reuses the array the first one left
+behind), at the parity tolerance of the other GPU tests, on the library's own
+kernel choice and on every kernel family that keeps records in the scratch.
+After each pair of calls the scratch's error latch must read 0.  The file is
+named so that pytest collects it last.
 """
 import ctypes
 
@@ -18,6 +21,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import oracle as orc
 from rl_triton import _native as nat
 
 pytestmark = pytest.mark.gpu
@@ -53,10 +57,18 @@ def _gae_noalloc(r, v, term, out):
 
 # Short rows (many rows per tile) and long rows (many tiles per row, so the
 # look-back carries values through the fixed scratch).
+# The kernel families: the library's choice (auto), and forced families whose
+# look-back records live in the scratch (tile, flat, flat2, flat3) or that use
+# it for segment maps (vrows).
+@pytest.mark.parametrize("path", ["auto", "tile", "flat", "flat2", "flat3", "vrows"])
 @pytest.mark.parametrize("n,t", [(4096, 128), (3, 70001), (1, 1 << 20)])
-def test_noalloc_matches_workspace_entry_point_twice(n, t):
+def test_noalloc_matches_workspace_entry_point_twice(n, t, path, monkeypatch):
     if not torch.cuda.is_available():
         pytest.fail("CUDA device required for -m gpu tests")
+    if path == "auto":
+        monkeypatch.delenv("RLS_PATH", raising=False)
+    else:
+        monkeypatch.setenv("RLS_PATH", path)
     for call in range(2):
         r, v, term = _inputs(n, t, seed=100 * call + n + t)
         want = torch.empty(n, t, device="cuda")
@@ -64,8 +76,13 @@ def test_noalloc_matches_workspace_entry_point_twice(n, t):
         _gae_with_workspace(r, v, term, want)
         _gae_noalloc(r, v, term, got)
         torch.cuda.synchronize()
-        np.testing.assert_allclose(got.cpu().numpy(), want.cpu().numpy(), rtol=RTOL, atol=ATOL,
-                                   err_msg=f"call {call}")
+        g = got.cpu().numpy()
+        np.testing.assert_allclose(g, want.cpu().numpy(), rtol=RTOL, atol=ATOL, err_msg=f"call {call}")
+        rn, vn, tn = (x.cpu().numpy() for x in (r, v, term))
+        np.testing.assert_allclose(g, orc.gae(rn, vn, tn, gamma=0.99, lam=0.95), rtol=RTOL, atol=ATOL,
+                                   err_msg=f"call {call} vs oracle")
+    stream = torch.cuda.current_stream().cuda_stream
+    assert nat.lib.rls_gae_noalloc_error(ctypes.c_void_p(stream)) == 0
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
