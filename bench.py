@@ -360,9 +360,14 @@ def cpu_sample(cfg, budget_s=15.0, max_steps=50):
 
 # --------------------------------------------------------------------------
 def input_sets(cfg):
-    """Input sets rotated between steps so the working set exceeds the 126 MB L2."""
+    """Input sets rotated between launches so that every function's own working
+    set (its bytes per launch x the sets) is at least 3x the 126 MB L2: a launch
+    then finds (almost) none of its inputs in L2 from the launches before it.
+    Capped at 64 sets and 12 GB of inputs."""
     per_set = sum(bytes_per_step(f, cfg["trunc"], cfg["bf16"]) for f in cfg["funcs"]) * cfg["N"] * cfg["T"]
-    n_sets = max(1, min(8, int(np.ceil(3 * 126e6 / per_set)))) if per_set < 3 * 126e6 else 1
+    min_fn = min(bytes_per_step(f, cfg["trunc"], cfg["bf16"]) for f in cfg["funcs"]) * cfg["N"] * cfg["T"]
+    n_sets = int(np.ceil(3 * 126e6 / min_fn))
+    n_sets = max(1, min(n_sets, 64, int(12e9 // per_set)))
     return n_sets, per_set
 
 
@@ -372,7 +377,9 @@ def config_dict(cfg, world, split, n_sets, per_set, use_graph):
             "seq_len": cfg["T"],
             "parallelism": (f"time-split x{world}" if split else f"env-sharded x{world}") if world > 1
             else "single GPU",
-            "l2": f"{n_sets} rotating input sets ({per_set * n_sets / 1e6:.0f} MB > 126 MB L2)",
+            "l2": f"{n_sets} rotating input sets ({per_set * n_sets / 1e6:.0f} MB; every function's own inputs "
+                  f"x {n_sets} >= 3x the 126 MB L2)" if n_sets > 1 else
+                  f"1 input set ({per_set / 1e6:.0f} MB, > 3x the 126 MB L2)",
             "launch": "CUDA graph per input set" if use_graph else "eager"}
 
 
@@ -697,8 +704,30 @@ def run_e2e(cfg, x0, dev, split, world, ksteps):
     a1.record(ds)
     torch.cuda.synchronize(dev)
     ms = max_over_ranks(a0.elapsed_time(a1) / ksteps, world)
+    # The copies alone (same buffers and streams, no calls): the floor of the step.
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cs):
+        c0.record(cs)
+        for k in range(ksteps):
+            for key in keys:
+                bufs[k % 2][key].copy_(host[key], non_blocking=True)
+        c1.record(cs)
+    res0 = make_calls(cfg, {**bufs[0], **const}, split)
+    outs = [o for f, c in res0.items() for o in flat_outputs(f, c()).values()]
+    torch.cuda.synchronize(dev)
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(ds):
+        d0.record(ds)
+        for k in range(ksteps):
+            for o, r in zip(pinned[k % 2], outs):
+                o.copy_(r, non_blocking=True)
+        d1.record(ds)
+    torch.cuda.synchronize(dev)
+    h2d_ms, d2h_ms = c0.elapsed_time(c1) / ksteps, d0.elapsed_time(d1) / ksteps
     return {"value": world * cfg["N"] * cfg["T"] / (ms / 1e3), "unit": "timesteps/s", "ms_per_step": ms,
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "copies_alone_ms": {"h2d": round(h2d_ms, 4), "d2h": round(d2h_ms, 4),
+                                "h2d_gbs": round(h2d / h2d_ms / 1e6, 1), "d2h_gbs": round(d2h / d2h_ms / 1e6, 1)},
             "path": "rl_triton public API; pinned host buffers; per step H2D of every input, the calls, D2H of "
                     "every output; copies in / calls / copies out on three streams, two buffer sets"}
 

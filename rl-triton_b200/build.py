@@ -19,6 +19,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "rl_triton", "_lib")
 LIB = os.path.join(LIBDIR, "librlscan.so")
+TORCH_LIB = os.path.join(LIBDIR, "librlscan_torch.so")
 SOURCES = ["rlscan.cu", "segment.cu"]
 HEADERS = ["common.cuh", "algs.cuh", "scan_kernel.cuh", "rows_kernel.cuh", "rows2_kernel.cuh", "tile_kernel.cuh", "tile_policies.cuh"]
 
@@ -52,12 +53,46 @@ def _stale() -> bool:
     return any(os.path.getmtime(d) > t for d in deps)
 
 
+def torch_flags() -> list[str]:
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    inc = [os.path.join(os.path.dirname(torch.__file__), "include"),
+           os.path.join(os.path.dirname(torch.__file__), "include", "torch", "csrc", "api", "include"),
+           os.path.join(os.path.dirname(os.path.dirname(nvcc_path())), "include")]
+    libdir = ce.library_paths()[0]
+    abi = "1" if torch.compiled_with_cxx11_abi() else "0"
+    return ([f"-I{d}" for d in inc] + ["-I", os.path.join(ROOT, "include"), f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+                                       "-DTORCH_API_INCLUDE_EXTENSION_H=0"],
+            [f"-L{libdir}", f"-Wl,-rpath,{libdir}", f"-L{LIBDIR}", "-Wl,-rpath,$ORIGIN", "-lrlscan", "-lc10",
+             "-lc10_cuda", "-ltorch_cpu", "-ltorch"])
+
+
+def build_torch_ops(force: bool = False) -> str:
+    """librlscan_torch.so: the rl_triton::* PyTorch operators (torch_ops.cpp),
+    linked against librlscan.so."""
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    if (not force and os.path.exists(TORCH_LIB) and os.path.getmtime(TORCH_LIB) > os.path.getmtime(src)
+            and os.path.getmtime(TORCH_LIB) > os.path.getmtime(LIB)):
+        return TORCH_LIB
+    cflags, ldflags = torch_flags()
+    tmp = TORCH_LIB + ".tmp"
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", *cflags, src, "-o", tmp, *ldflags]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        sys.stderr.write(res.stdout + res.stderr)
+        raise RuntimeError("g++ failed building librlscan_torch.so")
+    os.replace(tmp, TORCH_LIB)
+    return TORCH_LIB
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
+        build_torch_ops()
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
     tmp = LIB + ".tmp"
-    cmd = [nvcc_path(), *nvcc_flags(verbose), "-shared", "-o", tmp]
+    cmd = [nvcc_path(), *nvcc_flags(verbose), "-shared", "-Xlinker", "-soname=librlscan.so", "-o", tmp]
     cmd += [os.path.join(CSRC, f) for f in SOURCES]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
@@ -66,6 +101,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if verbose:
         sys.stderr.write(res.stderr)
     os.replace(tmp, LIB)
+    build_torch_ops(force=True)
     return LIB
 
 
@@ -73,5 +109,9 @@ if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--verbose", action="store_true", help="print ptxas register/spill report")
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--torch-only", action="store_true", help="rebuild only librlscan_torch.so")
     a = ap.parse_args()
-    print(build(force=a.force or a.verbose, verbose=a.verbose))
+    if a.torch_only:
+        print(build_torch_ops(force=True))
+    else:
+        print(build(force=a.force or a.verbose, verbose=a.verbose))

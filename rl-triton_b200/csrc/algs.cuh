@@ -41,6 +41,10 @@ struct Geom {
   int smem_per_warp;  // dynamic shared memory per warp (Retrace staging)
   int tma;            // 1: staging uses cp.async.bulk
   int l2_prefetch;    // flat3: bulk L2 prefetch of each super-tile before its first walk
+  int pdl;            // row kernels launched with programmatic stream serialization:
+                      // 0 none; 1 wait for the preceding kernel before the first load;
+                      // 2 issue the first chunk's loads, then wait (inputs are not
+                      //   outputs of the preceding library launch on this stream)
 };
 
 // Struct-generic warp shuffles for neighbour records (all 32-bit members).

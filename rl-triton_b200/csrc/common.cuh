@@ -188,6 +188,16 @@ __device__ __forceinline__ void store_run(float* p, int64_t i, int64_t M, bool f
 // invariant shows up as a host-visible status, never as a hung GPU.
 constexpr unsigned kSpinLimit = 1u << 22;  // ~0.3 s with the nanosleep back-off
 
+// ---- programmatic dependent launch ------------------------------------------
+// A kernel launched with cudaLaunchAttributeProgrammaticStreamSerialization may
+// start while the kernel before it on the stream is still running.  It must
+// execute pdl_wait() (griddepcontrol.wait: the preceding grid has completed and
+// its memory is visible) before it reads anything that grid may have written
+// and before its first store; pdl_trigger() lets the next such kernel launch.
+// Both are no-ops for a kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- host: pointer placement and device guard ------------------------------
 // Every entry point checks, before it enqueues anything, that each non-null
 // array argument is memory of one CUDA device (device or managed memory, not

@@ -9,6 +9,7 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <utility>
 
 #include "rlscan.h"
 #include "scan_kernel.cuh"
@@ -107,6 +108,89 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
 }
 
+// ---- programmatic dependent launch of the row kernels ------------------------
+// The row kernels (one warp per row, no workspace) are launched with
+// programmatic stream serialization: the next one's launch and CTA ramp overlap
+// the tail of the one before, which at 4096 x 128 is most of a launch.  A
+// kernel waits (griddepcontrol.wait) for the preceding grid before its first
+// store, and before its first load unless none of its inputs can be an output
+// of the preceding library launch on the stream.  Only the row kernels trigger
+// their dependents early; any other preceding kernel (this library's or not)
+// completes before a dependent starts, so the overlap check needs only the
+// outputs of the last row-kernel launch per stream, kept here under the launch
+// lock.
+struct PdlRange {
+  uintptr_t lo, hi;
+};
+struct PdlRecord {
+  cudaStream_t s;
+  PdlRange out[2];
+  bool used;
+};
+PdlRecord g_pdl[64];
+int g_pdl_next = 0;
+
+PdlRecord* pdl_find(cudaStream_t s) {
+  for (auto& r : g_pdl)
+    if (r.used && r.s == s) return &r;
+  return nullptr;
+}
+
+struct PdlIn {
+  const void* p;
+  size_t bytes;
+};
+// 2: the inputs are disjoint from the last row-kernel outputs on this stream
+// (loads may start before the wait); 1: they may overlap (wait first).
+int pdl_mode(cudaStream_t s, std::initializer_list<PdlIn> ins) {
+  const PdlRecord* r = pdl_find(s);
+  if (!r) return 2;
+  for (const PdlIn& in : ins) {
+    if (!in.p || !in.bytes) continue;
+    const uintptr_t lo = (uintptr_t)in.p, hi = lo + in.bytes;
+    for (const PdlRange& o : r->out)
+      if (o.lo < hi && lo < o.hi) return 1;
+  }
+  return 2;
+}
+
+void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes) {
+  PdlRecord* r = pdl_find(s);
+  if (!r) {
+    r = &g_pdl[g_pdl_next];
+    g_pdl_next = (g_pdl_next + 1) % 64;
+    r->s = s;
+    r->used = true;
+  }
+  r->out[0] = PdlRange{(uintptr_t)out0, out0 ? (uintptr_t)out0 + bytes : 0};
+  r->out[1] = PdlRange{(uintptr_t)out1, out1 ? (uintptr_t)out1 + bytes : 0};
+}
+
+// Launch a row kernel: plain when g.pdl == 0, else with the PDL attribute.
+template <class... KArgs, class... Args>
+int launch_rowk(void (*kern)(KArgs...), int64_t blocks, int threads, cudaStream_t s, const Geom& g,
+                const float* out0, const float* out1, Args&&... args) {
+  if (blocks > 0x7fffffffLL) return RLS_EINVAL;
+  if (g.pdl == 0) {
+    kern<<<(unsigned)blocks, threads, 0, s>>>(std::forward<Args>(args)...);
+    if (cudaPeekAtLastError() != cudaSuccess) return RLS_ECUDA;
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)blocks);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) return RLS_ECUDA;
+  }
+  pdl_record(s, out0, out1, (size_t)g.M * sizeof(float));
+  return RLS_OK;
+}
+
 // ---- row-parallel path ------------------------------------------------
 constexpr int kRowWarps = 4;  // rows (warps) per CTA of the row kernel
 
@@ -125,9 +209,7 @@ bool use_rows(const Geom& g) {
 template <class Alg, int R>
 int launch_rows_r(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
   const int64_t blocks = (g.N + kRowWarps - 1) / kRowWarps;
-  if (blocks > 0x7fffffffLL) return RLS_EINVAL;
-  rows_kernel<Alg, kRowWarps, R><<<(unsigned)blocks, kRowWarps * 32, 0, s>>>(p, g);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  return launch_rowk(rows_kernel<Alg, kRowWarps, R>, blocks, kRowWarps * 32, s, g, p.out0, p.out1, p, g);
 }
 
 // Rounds per chunk: enough 16-byte vectors in flight per lane without
@@ -289,10 +371,8 @@ struct Rows2L {
     const int forced = env_int("RLS_ROWS2_R", 0);
     const int r = forced ? forced : 1;  // one round per chunk: the leanest registers measured fastest
     const int64_t blocks = (g.N + 3) / 4;
-    if (blocks > 0x7fffffffLL) return RLS_EINVAL;
-    if (r >= 2) rows2_kernel<P, 4, 2><<<(unsigned)blocks, 128, 0, s>>>(p, g);
-    else rows2_kernel<P, 4, 1><<<(unsigned)blocks, 128, 0, s>>>(p, g);
-    return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+    if (r >= 2) return launch_rowk(rows2_kernel<P, 4, 2>, blocks, 128, s, g, p.out0, p.out1, p, g);
+    return launch_rowk(rows2_kernel<P, 4, 1>, blocks, 128, s, g, p.out0, p.out1, p, g);
   }
 };
 
@@ -601,6 +681,8 @@ int make_geom(int64_t N, int64_t T, const rls_segment_t* seg, bool backward, Geo
   g.edge_global = 1;
   g.smem_per_warp = 0;
   g.tma = 0;
+  g.l2_prefetch = 0;
+  g.pdl = 0;
   if (seg) {
     if (seg->t0 < 0 || seg->total_len < seg->t0 + T) return RLS_EINVAL;
     g.seg = 1;
@@ -697,6 +779,9 @@ int rls_gae(const void* rewards, const void* values, const void* terminateds, co
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  const size_t esz = in_dtype == RLS_BF16 ? 2 : 4, mb = (size_t)g.M * esz, nb = (size_t)g.N * 4;
+  g.pdl = pdl_mode(s, {{rewards, mb}, {values, mb}, {terminateds, mb}, {truncateds, mb},
+                      {bootstrap, boot_kind == RLS_BOOT_ROW ? nb : mb}, {seg ? seg->halo : nullptr, nb}});
   const float gl = gamma * lambda_;
 #define GAE_PARAMS(T)                                                                                     \
   typename GaeAlg<T>::Params p;                                                                           \
@@ -755,6 +840,9 @@ int rls_vtrace(const void* log_pi_target, const void* log_pi_behavior, const voi
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  const size_t esz = in_dtype == RLS_BF16 ? 2 : 4, mb = (size_t)g.M * esz, nb = (size_t)g.N * 4;
+  g.pdl = pdl_mode(s, {{log_pi_target, mb}, {log_pi_behavior, mb}, {values, mb}, {rewards, mb},
+                      {terminateds, mb}, {truncateds, mb}, {bootstrap, boot_kind == RLS_BOOT_ROW ? nb : mb}});
 #define VT_PARAMS(T)                                                                                      \
   typename VtraceAlg<T>::Params p;                                                                        \
   p.lpt = (const T*)log_pi_target; p.lpb = (const T*)log_pi_behavior; p.v = (const T*)values;              \
@@ -811,6 +899,12 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  {
+    const size_t m4 = (size_t)g.M * 4, ma = m4 * (size_t)num_actions;
+    g.pdl = pdl_mode(s, {{action_probs_target, ma}, {action_probs_behavior, m4}, {q_values, m4},
+                         {next_q_values_all, ma}, {actions, 2 * m4}, {rewards, m4}, {terminateds, m4},
+                         {truncateds, m4}});
+  }
   RetraceAlg::Params p;
   p.pi = action_probs_target; p.mu = action_probs_behavior; p.q = q_values; p.nq = next_q_values_all;
   p.act = actions; p.r = rewards; p.term = terminateds; p.trunc = truncateds;
@@ -862,6 +956,9 @@ int rls_lambda_returns(const void* rewards, const void* next_values, const void*
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  const size_t esz = in_dtype == RLS_BF16 ? 2 : 4, mb = (size_t)g.M * esz, nb = (size_t)g.N * 4;
+  g.pdl = pdl_mode(s, {{rewards, mb}, {next_values, mb}, {terminateds, mb}, {truncateds, mb},
+                      {bootstrap, mb}, {seg ? seg->halo : nullptr, nb}});
 #define LAM_PARAMS(T)                                                                                     \
   typename LambdaAlg<T>::Params p;                                                                        \
   p.r = (const T*)rewards; p.nv = (const T*)next_values; p.term = (const T*)terminateds;                   \
@@ -913,6 +1010,9 @@ int rls_discounted_returns(const void* rewards, const void* terminateds, const v
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  const size_t esz = in_dtype == RLS_BF16 ? 2 : 4, mb = (size_t)g.M * esz, nb = (size_t)g.N * 4;
+  g.pdl = pdl_mode(s, {{rewards, mb}, {terminateds, mb}, {truncateds, mb}, {bootstrap, mb},
+                      {seg ? seg->halo : nullptr, nb}});
 #define DISC_PARAMS(T)                                                                                    \
   typename DiscountedAlg<T>::Params p;                                                                    \
   p.r = (const T*)rewards; p.term = (const T*)terminateds; p.trunc = (const T*)truncateds;                 \
@@ -958,6 +1058,8 @@ static int forward_common(const void* x, const void* dones, const float* seed, f
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  const size_t esz = in_dtype == RLS_BF16 ? 2 : 4, mb = (size_t)g.M * esz, nb = (size_t)g.N * 4;
+  g.pdl = pdl_mode(s, {{x, mb}, {dones, mb}, {seed, nb}, {seg ? seg->halo : nullptr, nb}});
 #define FWD_PARAMS(T)                                                                                     \
   typename ForwardAlg<T>::Params p;                                                                       \
   p.x = (const T*)x; p.done = (const T*)dones; p.seed = seed; p.halo = seg ? seg->halo : nullptr;          \
@@ -1016,6 +1118,8 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
   if (st) return st;
   cudaStream_t s = as_stream(stream);
   std::lock_guard<std::recursive_mutex> launch_lock(launch_mutex());
+  g.pdl = pdl_mode(s, {{u, (size_t)g.M * 4}, {v, (size_t)g.M * 4}, {carry, (size_t)g.N * 4},
+                      {seg ? seg->halo : nullptr, (size_t)g.N * 4}});
   if (direction == 0) {
     AffineAlg<true>::Params p{u, v, carry, out, nullptr};
     {

@@ -267,7 +267,10 @@ __global__ void __launch_bounds__(WPB * 32) rows2_kernel(const typename P::Param
   Rows2Chunk<P, R> a, b;
   typename P::Nbr edge_nbr{};
   float carry = 0.f;
+  pdl_trigger();
+  if (g.pdl == 1) pdl_wait();
   rows2_load<P, R>(p, rbase, S, cb_of(0), lane, a);
+  if (g.pdl == 2) pdl_wait();  // the first chunk's loads are in flight; no store before this
   for (int64_t k = 0; k < nch; k += 2) {
     if (k + 1 < nch) rows2_load<P, R>(p, rbase, S, cb_of(k + 1), lane, b);
     carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k), lane, a, carry, edge_nbr);

@@ -45,6 +45,8 @@ rows_kernel(const typename Alg::Params p, const Geom g) {
 
   float carry = 0.f;  // state entering the chunk (edges fold the boundary in)
   Nbr edge_nbr{};     // neighbour across the chunk edge, from the previous chunk
+  pdl_trigger();
+  if (g.pdl == 1) pdl_wait();
 
   for (int64_t k = 0; k < nch; ++k) {
     const int64_t c = BWD ? (nch - 1 - k) : k;
@@ -58,6 +60,7 @@ rows_kernel(const typename Alg::Params p, const Geom g) {
       if (col + VEC <= S) Alg::load(p, i, rend, true, run[r], nullptr, 0);
       else Alg::load(p, i, rend, false, run[r], nullptr, 0);
     }
+    if (g.pdl == 2 && k == 0) pdl_wait();  // the first loads are in flight; no store before this
 
     Nbr halo[ROUNDS];
     if constexpr (Alg::kNeedsNbr) {

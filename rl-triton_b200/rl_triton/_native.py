@@ -8,7 +8,6 @@ from __future__ import annotations
 
 import ctypes
 import os
-import threading
 
 import torch
 
@@ -54,6 +53,60 @@ def _load() -> ctypes.CDLL:
 
 lib = _load()
 
+TORCH_LIB_PATH = os.path.join(os.path.dirname(LIB_PATH), "librlscan_torch.so")
+if not os.path.exists(TORCH_LIB_PATH):
+    raise ImportError(f"librlscan_torch.so not found at {TORCH_LIB_PATH}; build it with "
+                      "`python rl-triton_b200/build.py`")
+torch.ops.load_library(TORCH_LIB_PATH)
+ops = torch.ops.rl_triton  # the estimators as PyTorch operators (csrc/torch_ops.cpp)
+
+
+# Fake (meta) kernels: output shapes and dtypes without running anything, so
+# torch.compile can trace through the operators.
+def _f32_like(t):
+    return torch.empty(t.shape, dtype=torch.float32, device=t.device)
+
+
+@torch.library.register_fake("rl_triton::gae")
+def _(rewards, values, terminateds, truncateds, bootstrap, boot_kind, gamma, lambda_, t0=-1, total=-1, halo=None):
+    return _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::vtrace")
+def _(lpt, lpb, values, rewards, terminateds, truncateds, bootstrap, boot_kind, gamma, rho_bar, c_bar):
+    return _f32_like(rewards), _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::retrace")
+def _(pi, mu, q, nq, actions, rewards, terminateds, truncateds, gamma, lambda_, c_bar, rho_bar):
+    return _f32_like(rewards), _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::lambda_returns")
+def _(rewards, next_values, terminateds, truncateds, bootstrap, boot_kind, gamma, lambda_, t0=-1, total=-1,
+      halo=None):
+    return _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::discounted_returns")
+def _(rewards, terminateds, truncateds, bootstrap, boot_kind, gamma, t0=-1, total=-1, halo=None):
+    return _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::eligibility_traces")
+def _(gradients, dones, seed_values, gamma, lambda_, t0=-1, total=-1, halo=None):
+    return _f32_like(gradients)
+
+
+@torch.library.register_fake("rl_triton::prefix_sum")
+def _(inputs, dones, seed_values, ends_at, t0=-1, total=-1, halo=None):
+    return _f32_like(inputs)
+
+
+@torch.library.register_fake("rl_triton::affine_scan")
+def _(u, v, carry, direction, t0=-1, total=-1, halo=None):
+    return _f32_like(u)
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _F = ctypes.c_float
@@ -94,7 +147,8 @@ def check(status: int, what: str, device: torch.device | None = None) -> None:
     if status != RLS_OK:
         msg = lib.rls_status_string(status).decode()
         raise RuntimeError(f"{what}: librlscan status {status} ({msg})")
-    if device is not None and os.environ.get("RL_TRITON_CORRECTNESS_WARNINGS", "0") == "1":
+    if (device is not None and os.environ.get("RL_TRITON_CORRECTNESS_WARNINGS", "0") == "1"
+            and not torch.cuda.is_current_stream_capturing()):  # a capture cannot synchronise
         raise_if_device_error(device)
 
 
@@ -115,38 +169,25 @@ def stream_handle(device: torch.device) -> int:
 
 
 # ---------------------------------------------------------------------------
-# Per-(device, stream) workspace: tile status words for the decoupled
-# look-back.  Zero-filled once at allocation; the kernels keep it consistent
-# across calls on the same stream (an epoch counter lives in its header).
+# Per-(device, stream) workspace: tile records for the decoupled look-back.
+# Owned by the operator library (one cache for every caller); zero-filled once
+# at allocation, kept consistent across calls on the same stream by the
+# kernels (an epoch counter lives in its header).
 # ---------------------------------------------------------------------------
-_ws_lock = threading.Lock()
-_ws_cache: dict[tuple[int, int], torch.Tensor] = {}
-
-
 def workspace(device: torch.device, stream: int, num_elements: int) -> tuple[int, int]:
-    need = int(lib.rls_workspace_bytes(max(int(num_elements), 1)))
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    key = (idx, stream)
-    with _ws_lock:
-        buf = _ws_cache.get(key)
-        if buf is None or buf.numel() < need:
-            size = max(need, 1 << 16)
-            if buf is not None:
-                size = max(size, 2 * buf.numel())
-            buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", idx))
-            _ws_cache[key] = buf
+    """(pointer, bytes) of the current stream's workspace on `device`, large
+    enough for num_elements; for callers of the C ABI on that stream."""
+    like = torch.empty(0, device=device)
+    assert stream == stream_handle(like.device), "workspace() serves the device's current stream"
+    buf = ops.workspace(like, max(int(num_elements), 1))
     return buf.data_ptr(), buf.numel()
 
 
 def workspace_error(device: torch.device | None = None) -> int:
-    """Bounded-wait error latch of the current stream's workspace (syncs)."""
+    """Bounded-wait error latch of the current stream's workspace (syncs the
+    stream, clears the latch)."""
     device = device or torch.device("cuda", torch.cuda.current_device())
-    idx = device.index if device.index is not None else torch.cuda.current_device()
-    s = stream_handle(device)
-    buf = _ws_cache.get((idx, s))
-    if buf is None:
-        return 0
-    return int(lib.rls_workspace_error(ctypes.c_void_p(buf.data_ptr()), ctypes.c_void_p(s)))
+    return int(ops.workspace_error(torch.empty(0, device=device)))
 
 
 def raise_if_device_error(device: torch.device | None = None) -> None:

@@ -54,7 +54,7 @@ class CudaKernels:
     def scan(self, alg, x, seg: Segment, halo, p):
         import rl_triton
 
-        c = seg.cstruct(halo)
+        c = (seg.t0, seg.total, halo)
         if alg == GAE:
             return rl_triton.compute_gae(x["rewards"], x["values"], x["terminateds"], x.get("truncateds"),
                                          p["gamma"], p["lambda_"], last_value=x.get("last_value"), _segment=c)

@@ -30,7 +30,11 @@ _PERF_WARNINGS = os.environ.get("RL_TRITON_PERF_WARNINGS", "0") == "1"
 
 # Set RL_TRITON_CORRECTNESS_WARNINGS=1 to enable the expensive input checks
 # (read per call: src/rl_triton/ops/_scan.py:30-31).
+# Under torch.compile the data-dependent checks are skipped (they would
+# synchronise and break the graph).
 def _CORRECTNESS_WARNINGS() -> bool:
+    if torch.compiler.is_compiling():
+        return False
     return os.environ.get("RL_TRITON_CORRECTNESS_WARNINGS", "0") == "1"
 
 
@@ -53,52 +57,42 @@ def _float_ok(t: torch.Tensor) -> bool:
     return t.dtype in _FLOAT_DTYPES
 
 
-def _ready(t: torch.Tensor | None, name: str = "tensor") -> torch.Tensor | None:
-    """Contiguous and 16-byte aligned (the kernels use 128-bit accesses)."""
-    if t is None:
-        return None
-    if not t.is_contiguous():
-        _perf_warn(f"{name} is not contiguous; a copy will be made. Call .contiguous() before the hot loop to avoid this overhead.")
-        t = t.contiguous()
-    if t.data_ptr() % 16 != 0:
-        _perf_warn(f"{name} is not 16-byte aligned; a copy will be made.")
-        t = t.clone()
-    return t
-
-
-def _unify(streams: list[torch.Tensor | None]) -> tuple[list[torch.Tensor | None], int]:
-    """All [N, T] floating input streams of one call share one element type.
-
-    bf16 is used only when every stream is bf16; otherwise every stream is
-    promoted to fp32 (arithmetic is fp32 either way).
-    """
-    present = [s for s in streams if s is not None]
-    if present and all(s.dtype == torch.bfloat16 for s in present):
-        return streams, nat.RLS_BF16
-    out = [None if s is None else (s if s.dtype == torch.float32 else s.float()) for s in streams]
-    return out, nat.RLS_F32
-
-
-def _scalar_f32(t: torch.Tensor | None) -> torch.Tensor | None:
-    if t is None:
-        return None
-    if t.dtype != torch.float32:
-        t = t.float()
-    return _ready(t)
-
-
-def _launch_ctx(ref: torch.Tensor, *others: torch.Tensor | None) -> tuple[torch.device, int]:
-    """Device and current stream of a call, after the always-on placement
-    check: every tensor the kernel reads or writes is a CUDA tensor on the
-    same device as `ref` (the library checks the pointers again and returns
-    RLS_ENOTDEVICE before launching anything)."""
+def _placed(ref: torch.Tensor, *others: torch.Tensor | None) -> None:
+    """Always-on placement check: every tensor a kernel reads or writes is a
+    CUDA tensor on `ref`'s device (the library checks the pointers again and
+    refuses host memory before it launches anything)."""
     assert ref.is_cuda, "inputs must be on CUDA"
     dev = ref.device
     for t in others:
         if t is not None:
             assert t.is_cuda and t.device == dev, \
                 f"all tensors of one call must be on {dev}; got a tensor on {t.device}"
-    return dev, nat.stream_handle(dev)
+
+
+def _warn_copies(named: dict) -> None:
+    """RL_TRITON_PERF_WARNINGS=1: warn about the copies the operator will make
+    (non-contiguous or not 16-byte aligned inputs)."""
+    if not _PERF_WARNINGS:
+        return
+    for name, t in named.items():
+        if t is None:
+            continue
+        if not t.is_contiguous():
+            _perf_warn(f"{name} is not contiguous; a copy will be made. Call .contiguous() before the hot loop to avoid this overhead.")
+        elif t.data_ptr() % 16 != 0:
+            _perf_warn(f"{name} is not 16-byte aligned; a copy will be made.")
+
+
+def _done(ref: torch.Tensor) -> None:
+    """RL_TRITON_CORRECTNESS_WARNINGS=1: wait for the call and raise if one of
+    its bounded device waits ran out."""
+    if _CORRECTNESS_WARNINGS() and not torch.cuda.is_current_stream_capturing():
+        nat.raise_if_device_error(ref.device)
+
+
+def _seg(segment):
+    """(t0, total, halo) of a time-split call, or the whole-rows defaults."""
+    return segment if segment is not None else (-1, -1, None)
 
 
 def _run_scan(
@@ -167,18 +161,10 @@ def _run_scan_forward(
     return _affine(u, v, seed, direction=1)
 
 
-def _affine(u, v, carry, direction, segment=None, out=None):
-    u = _ready(u.float() if u.dtype != torch.float32 else u, "u")
-    v = _ready(v.float() if v.dtype != torch.float32 else v, "v")
-    carry = _scalar_f32(carry)
-    num_envs, seq_len = u.shape
-    if out is None:
-        out = torch.empty_like(u)
-    dev, s = _launch_ctx(u, v, carry, out)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_affine_scan(
-        u.data_ptr(), v.data_ptr(), nat.ptr(carry), direction, out.data_ptr(),
-        num_envs, seq_len, segment, ws, wsb, s,
-    )
-    nat.check(st, "rls_affine_scan", dev)
+def _affine(u, v, carry, direction, segment=None):
+    _placed(u, v, carry)
+    _warn_copies({"u": u, "v": v})
+    t0, total, halo = _seg(segment)
+    out = nat.ops.affine_scan(u, v, carry, direction, t0, total, halo)
+    _done(u)
     return out

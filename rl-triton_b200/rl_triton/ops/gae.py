@@ -4,15 +4,7 @@ from __future__ import annotations
 import torch
 
 from rl_triton import _native as nat
-from rl_triton.ops._scan import (
-    _CORRECTNESS_WARNINGS,
-    _FLAT_MAX_SEQ_LEN,
-    _float_ok,
-    _launch_ctx,
-    _ready,
-    _scalar_f32,
-    _unify,
-)
+from rl_triton.ops._scan import _CORRECTNESS_WARNINGS, _FLAT_MAX_SEQ_LEN, _done, _float_ok, _placed, _seg, _warn_copies
 
 
 def compute_gae(
@@ -107,22 +99,11 @@ def compute_gae(
     else:
         kind = nat.BOOT_NONE
 
-    (rewards, values, terminateds, truncateds, boot), dt = _unify(
-        [rewards, values, terminateds, truncateds, boot])
-    rewards = _ready(rewards, "rewards")
-    values = _ready(values, "values")
-    terminateds = _ready(terminateds, "terminateds")
-    truncateds = _ready(truncateds, "truncateds")
-    boot = _ready(boot, "bootstrap_values")
-    row = _scalar_f32(last_value)
-
-    out = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    dev, s = _launch_ctx(rewards, values, terminateds, truncateds, boot, row, out)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_gae(
-        rewards.data_ptr(), values.data_ptr(), terminateds.data_ptr(), nat.ptr(truncateds),
-        nat.ptr(row if kind == nat.BOOT_ROW else boot), kind, out.data_ptr(),
-        num_envs, seq_len, float(gamma), float(lambda_), dt, _segment, ws, wsb, s,
-    )
-    nat.check(st, "rls_gae", dev)
+    _placed(rewards, values, terminateds, truncateds, boot, last_value)
+    _warn_copies({"rewards": rewards, "values": values, "terminateds": terminateds, "truncateds": truncateds,
+                  "bootstrap_values": boot})
+    t0, total, halo = _seg(_segment)
+    out = nat.ops.gae(rewards, values, terminateds, truncateds, last_value if kind == nat.BOOT_ROW else boot, kind,
+                      float(gamma), float(lambda_), t0, total, halo)
+    _done(rewards)
     return out

@@ -4,13 +4,7 @@ from __future__ import annotations
 import torch
 
 from rl_triton import _native as nat
-from rl_triton.ops._scan import (
-    _CORRECTNESS_WARNINGS,
-    _launch_ctx,
-    _ready,
-    _scalar_f32,
-    _unify,
-)
+from rl_triton.ops._scan import _CORRECTNESS_WARNINGS, _done, _placed, _seg, _warn_copies
 
 
 def compute_episodic_prefix_sum(
@@ -53,16 +47,9 @@ def compute_episodic_prefix_sum(
     # The reference compiles any other string as "starts_at"
     # (BOUNDARY_ENDS_AT=(boundary == "ends_at"), ops/prefix_sum.py:110).
     ends_at = 1 if boundary == "ends_at" else 0
-    (inputs, dones), dt = _unify([inputs, dones])
-    inputs = _ready(inputs, "inputs")
-    dones = _ready(dones, "dones")
-    seed = _scalar_f32(seed_values)
-    out = torch.empty(inputs.shape, dtype=torch.float32, device=inputs.device)
-    dev, s = _launch_ctx(inputs, dones, seed, out)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_prefix_sum(
-        inputs.data_ptr(), dones.data_ptr(), nat.ptr(seed), ends_at, out.data_ptr(),
-        num_envs, seq_len, dt, _segment, ws, wsb, s,
-    )
-    nat.check(st, "rls_prefix_sum", dev)
+    _placed(inputs, dones, seed_values)
+    _warn_copies({"inputs": inputs, "dones": dones})
+    t0, total, halo = _seg(_segment)
+    out = nat.ops.prefix_sum(inputs, dones, seed_values, bool(ends_at), t0, total, halo)
+    _done(inputs)
     return out

@@ -10,33 +10,20 @@ from __future__ import annotations
 import torch
 
 from rl_triton import _native as nat
-from rl_triton.ops._scan import _launch_ctx, _ready
+from rl_triton.ops._scan import _done, _placed, _warn_copies
 
 
 def _retrace_launch(action_probs_target, action_probs_behavior, q_values, next_q_values_all, actions,
                     rewards, truncateds, terminateds, gamma, lambda_, c_bar, rho_bar):
-    num_envs, seq_len = rewards.shape
-    num_actions = action_probs_target.shape[2]
-    f = lambda t, n: _ready(t if t.dtype == torch.float32 else t.float(), n)  # noqa: E731
-    pi = f(action_probs_target, "action_probs_target")
-    mu = f(action_probs_behavior, "action_probs_behavior")
-    q = f(q_values, "q_values")
-    nq = f(next_q_values_all, "next_q_values_all")
-    act = _ready(actions, "actions")
-    r = f(rewards, "rewards")
-    term = f(terminateds, "terminateds")
-    trunc = f(truncateds, "truncateds")
-    targets = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    advantages = torch.empty_like(targets)
-    dev, s = _launch_ctx(rewards, pi, mu, q, nq, act, term, trunc, targets, advantages)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_retrace(
-        pi.data_ptr(), mu.data_ptr(), q.data_ptr(), nq.data_ptr(), act.data_ptr(), r.data_ptr(),
-        term.data_ptr(), trunc.data_ptr(), targets.data_ptr(), advantages.data_ptr(),
-        num_envs, seq_len, num_actions, float(gamma), float(lambda_), float(c_bar), float(rho_bar),
-        ws, wsb, s,
-    )
-    nat.check(st, "rls_retrace", dev)
+    _placed(rewards, action_probs_target, action_probs_behavior, q_values, next_q_values_all, actions, terminateds,
+            truncateds)
+    _warn_copies({"action_probs_target": action_probs_target, "action_probs_behavior": action_probs_behavior,
+                  "q_values": q_values, "next_q_values_all": next_q_values_all, "actions": actions,
+                  "rewards": rewards, "terminateds": terminateds, "truncateds": truncateds})
+    targets, advantages = nat.ops.retrace(action_probs_target, action_probs_behavior, q_values, next_q_values_all,
+                                          actions, rewards, terminateds, truncateds, float(gamma), float(lambda_),
+                                          float(c_bar), float(rho_bar))
+    _done(rewards)
     return targets, advantages
 
 

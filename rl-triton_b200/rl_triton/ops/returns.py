@@ -5,14 +5,7 @@ from __future__ import annotations
 import torch
 
 from rl_triton import _native as nat
-from rl_triton.ops._scan import (
-    _CORRECTNESS_WARNINGS,
-    _float_ok,
-    _launch_ctx,
-    _ready,
-    _scalar_f32,
-    _unify,
-)
+from rl_triton.ops._scan import _CORRECTNESS_WARNINGS, _done, _float_ok, _placed, _seg, _warn_copies
 
 
 def _boot_kind(has_truncations: bool, bootstrap_values) -> int:
@@ -75,22 +68,13 @@ def compute_lambda_returns(
                 "terminated and truncated are mutually exclusive: a step cannot be both"
 
     kind = _boot_kind(has_truncations, bootstrap_values)
-    (rewards, next_values, terminateds, truncateds, boot), dt = _unify(
-        [rewards, next_values, terminateds, truncateds, bootstrap_values])
-    rewards = _ready(rewards, "rewards")
-    next_values = _ready(next_values, "next_values")
-    terminateds = _ready(terminateds, "terminateds")
-    truncateds = _ready(truncateds, "truncateds")
-    boot = _ready(boot, "bootstrap_values")
-    out = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    dev, s = _launch_ctx(rewards, next_values, terminateds, truncateds, boot, out)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_lambda_returns(
-        rewards.data_ptr(), next_values.data_ptr(), terminateds.data_ptr(), nat.ptr(truncateds),
-        nat.ptr(boot), kind, out.data_ptr(), num_envs, seq_len, float(gamma), float(lambda_), dt,
-        _segment, ws, wsb, s,
-    )
-    nat.check(st, "rls_lambda_returns", dev)
+    _placed(rewards, next_values, terminateds, truncateds, bootstrap_values)
+    _warn_copies({"rewards": rewards, "next_values": next_values, "terminateds": terminateds,
+                  "truncateds": truncateds, "bootstrap_values": bootstrap_values})
+    t0, total, halo = _seg(_segment)
+    out = nat.ops.lambda_returns(rewards, next_values, terminateds, truncateds, bootstrap_values, kind, float(gamma),
+                                 float(lambda_), t0, total, halo)
+    _done(rewards)
     return out
 
 
@@ -123,19 +107,13 @@ def compute_discounted_returns(
                 "terminated and truncated are mutually exclusive: a step cannot be both"
 
     kind = _boot_kind(has_truncations, bootstrap_values)
-    (rewards, terminateds, truncateds, boot), dt = _unify([rewards, terminateds, truncateds, bootstrap_values])
-    rewards = _ready(rewards, "rewards")
-    terminateds = _ready(terminateds, "terminateds")
-    truncateds = _ready(truncateds, "truncateds")
-    boot = _ready(boot, "bootstrap_values")
-    out = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    dev, s = _launch_ctx(rewards, terminateds, truncateds, boot, out)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_discounted_returns(
-        rewards.data_ptr(), terminateds.data_ptr(), nat.ptr(truncateds), nat.ptr(boot), kind,
-        out.data_ptr(), num_envs, seq_len, float(gamma), dt, _segment, ws, wsb, s,
-    )
-    nat.check(st, "rls_discounted_returns", dev)
+    _placed(rewards, terminateds, truncateds, bootstrap_values)
+    _warn_copies({"rewards": rewards, "terminateds": terminateds, "truncateds": truncateds,
+                  "bootstrap_values": bootstrap_values})
+    t0, total, halo = _seg(_segment)
+    out = nat.ops.discounted_returns(rewards, terminateds, truncateds, bootstrap_values, kind, float(gamma), t0,
+                                     total, halo)
+    _done(rewards)
     return out
 
 
@@ -172,16 +150,9 @@ def compute_eligibility_traces(
             f"seed_values must have shape [{num_envs}], got {seed_values.shape}"
         assert seed_values.is_cuda, "seed_values must be on CUDA"
 
-    (gradients, dones), dt = _unify([gradients, dones])
-    gradients = _ready(gradients, "gradients")
-    dones = _ready(dones, "dones")
-    seed = _scalar_f32(seed_values)
-    out = torch.empty(gradients.shape, dtype=torch.float32, device=gradients.device)
-    dev, s = _launch_ctx(gradients, dones, seed, out)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_eligibility_traces(
-        gradients.data_ptr(), dones.data_ptr(), nat.ptr(seed), out.data_ptr(), num_envs, seq_len,
-        float(gamma), float(lambda_), dt, _segment, ws, wsb, s,
-    )
-    nat.check(st, "rls_eligibility_traces", dev)
+    _placed(gradients, dones, seed_values)
+    _warn_copies({"gradients": gradients, "dones": dones})
+    t0, total, halo = _seg(_segment)
+    out = nat.ops.eligibility_traces(gradients, dones, seed_values, float(gamma), float(lambda_), t0, total, halo)
+    _done(gradients)
     return out

@@ -9,15 +9,7 @@ from __future__ import annotations
 import torch
 
 from rl_triton import _native as nat
-from rl_triton.ops._scan import (
-    _CORRECTNESS_WARNINGS,
-    _FLAT_MAX_SEQ_LEN,
-    _float_ok,
-    _launch_ctx,
-    _ready,
-    _scalar_f32,
-    _unify,
-)
+from rl_triton.ops._scan import _CORRECTNESS_WARNINGS, _FLAT_MAX_SEQ_LEN, _done, _float_ok, _placed, _warn_copies
 
 
 def _vtrace_launch(log_pi_target, log_pi_behavior, values, rewards, terminateds, truncateds,
@@ -37,29 +29,14 @@ def _vtrace_launch(log_pi_target, log_pi_behavior, values, rewards, terminateds,
     else:
         kind = nat.BOOT_NONE
 
-    (lpt, lpb, values, rewards, terminateds, truncateds, boot), dt = _unify(
-        [log_pi_target, log_pi_behavior, values, rewards, terminateds, truncateds, boot])
-    lpt = _ready(lpt, "log_pi_target")
-    lpb = _ready(lpb, "log_pi_behavior")
-    values = _ready(values, "values")
-    rewards = _ready(rewards, "rewards")
-    terminateds = _ready(terminateds, "terminateds")
-    truncateds = _ready(truncateds, "truncateds")
-    boot = _ready(boot, "bootstrap_values")
-    row = _scalar_f32(last_value)
-
-    targets = torch.empty(rewards.shape, dtype=torch.float32, device=rewards.device)
-    advantages = torch.empty_like(targets)
-    dev, s = _launch_ctx(rewards, lpt, lpb, values, terminateds, truncateds, boot, row, targets, advantages)
-    ws, wsb = nat.workspace(dev, s, num_envs * seq_len)
-    st = nat.lib.rls_vtrace(
-        lpt.data_ptr(), lpb.data_ptr(), values.data_ptr(), rewards.data_ptr(),
-        terminateds.data_ptr(), nat.ptr(truncateds),
-        nat.ptr(row if kind == nat.BOOT_ROW else boot), kind,
-        targets.data_ptr(), advantages.data_ptr(), num_envs, seq_len,
-        float(gamma), float(rho_bar), float(c_bar), dt, ws, wsb, s,
-    )
-    nat.check(st, "rls_vtrace", dev)
+    _placed(rewards, log_pi_target, log_pi_behavior, values, terminateds, truncateds, boot, last_value)
+    _warn_copies({"log_pi_target": log_pi_target, "log_pi_behavior": log_pi_behavior, "values": values,
+                  "rewards": rewards, "terminateds": terminateds, "truncateds": truncateds,
+                  "bootstrap_values": boot})
+    targets, advantages = nat.ops.vtrace(log_pi_target, log_pi_behavior, values, rewards, terminateds, truncateds,
+                                         last_value if kind == nat.BOOT_ROW else boot, kind, float(gamma),
+                                         float(rho_bar), float(c_bar))
+    _done(rewards)
     return targets, advantages
 
 

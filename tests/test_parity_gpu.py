@@ -373,3 +373,48 @@ def test_virtual_row_fixup_paths(kernel_path):
         close(got, orc.eligibility_traces(x["r"], x["term"], 0.99, 0.95), msg=f"traces {n}x{t}")
         got = rl_triton.compute_gae(T(x["r"]), T(x["v"]), T(x["term"]), gamma=0.99, lambda_=0.95).cpu().numpy()
         close(got, orc.gae(x["r"], x["v"], x["term"]), msg=f"gae {n}x{t}")
+
+
+def test_chained_calls_read_the_previous_output():
+    """A call whose input is the previous call's output (and calls whose outputs
+    reuse freed memory) on one stream, eagerly and replayed from a CUDA graph:
+    the row kernels overlap consecutive launches, so a kernel that reads the
+    previous launch's output must wait for it."""
+    import rl_triton
+    x = rng_inputs(4096, 128, seed=31, p_done=0.01)
+    r, term, v = T(x["r"]), T(x["term"]), T(x["v"])
+    d = (term > 0).float()
+
+    def chain():
+        a = rl_triton.compute_episodic_prefix_sum(r, d)
+        b = rl_triton.compute_discounted_returns(a, term, gamma=0.97)
+        c = rl_triton.compute_gae(b, a, term, gamma=0.99, lambda_=0.95)
+        e = rl_triton.compute_eligibility_traces(c, d, 0.99, 0.9)
+        return a, b, c, e
+
+    def oracle_chain(pr):
+        a = orc.prefix_sum(x["r"], x["term"], precision=pr)
+        b = orc.discounted_returns(a, x["term"], gamma=0.97, precision=pr)
+        c = orc.gae(b, a, x["term"], gamma=0.99, lam=0.95, precision=pr)
+        return a, b, c, orc.eligibility_traces(c, x["term"], 0.99, 0.9, precision=pr)
+
+    # Chained returns reach magnitudes ~10^3, where fp32 reassociation alone
+    # moves results by more than 1e-5: oracle.compare's fp64 criterion applies.
+    def check(outs, how):
+        for k, name in enumerate("abce"):
+            res = orc.compare(outs[k].cpu().numpy(), lambda pr: oracle_chain(pr)[k], RTOL, ATOL)
+            assert res["ok"], f"{how} {name}: {res}"
+
+    check(chain(), "eager")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        chain()  # workspace for this stream
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        outs = chain()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    check(outs, "graph")
