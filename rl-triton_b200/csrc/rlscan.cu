@@ -57,21 +57,11 @@ int prepare_layout(void* ws, size_t wsb, int layout, cudaStream_t s) {
   return RLS_OK;
 }
 
-int env_rounds() {
-  static int v = [] {
-    const char* s = std::getenv("RLS_ROUNDS");
-    if (!s) return 0;
-    int r = std::atoi(s);
-    return (r == 1 || r == 2 || r == 4) ? r : 0;
-  }();
-  return v;
-}
-
 // Rounds per warp: larger tiles for large inputs (fewer look-back hops, more
 // bytes in flight per thread); small inputs keep enough CTAs to fill 148 SMs.
 int pick_rounds(int64_t M, int vec, int max_rounds) {
-  int r = env_rounds();
-  if (!r) {
+  int r = 0;
+  {
     const int64_t per_round_tile = (int64_t)kWarps * 32 * vec;
     const int64_t tiles_r2 = (M + 2 * per_round_tile - 1) / (2 * per_round_tile);
     const int64_t tiles_r4 = (M + 4 * per_round_tile - 1) / (4 * per_round_tile);
@@ -194,10 +184,6 @@ int launch_rowk(void (*kern)(KArgs...), int64_t blocks, int threads, cudaStream_
 // ---- row-parallel path ------------------------------------------------
 constexpr int kRowWarps = 4;  // rows (warps) per CTA of the row kernel
 
-int env_int(const char* name, int dflt) {
-  const char* s = std::getenv(name);
-  return s ? std::atoi(s) : dflt;
-}
 
 // The row kernel needs every row to start on a 16-byte boundary; other shapes
 // fall back to the flat look-back kernel.
@@ -216,9 +202,8 @@ int launch_rows_r(const typename Alg::Params& p, const Geom& g, cudaStream_t s) 
 // padding short rows (a 128-step fp32 row is exactly one round).
 template <class Alg, int MAXR>
 int launch_rows(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
-  const int forced = env_int("RLS_ROWS_ROUNDS", 0);
   const int64_t run = 32 * Alg::kVec;
-  int r = forced ? forced : (int)std::min<int64_t>((g.S + run - 1) / run, MAXR);
+  int r = (int)std::min<int64_t>((g.S + run - 1) / run, MAXR);
   if (r >= 4 && MAXR >= 4) return launch_rows_r<Alg, (MAXR >= 4 ? 4 : 1)>(p, g, s);
   if (r >= 2 && MAXR >= 2) return launch_rows_r<Alg, (MAXR >= 2 ? 2 : 1)>(p, g, s);
   return launch_rows_r<Alg, 1>(p, g, s);
@@ -298,8 +283,6 @@ int launch_tile_k(const typename P::Params& p, TileGeom tg, void* ws, size_t ws_
       return RLS_ECUDA;
     if (dev < 64) { occ_smem[dev] = smem; occ_val[dev] = per_sm; }
   }
-  const int cap_env = env_int("RLS_TILE_CTAS_PER_SM", 0);
-  if (cap_env > 0 && cap_env < per_sm) per_sm = cap_env;
   int64_t grid = (int64_t)per_sm * num_sms(dev);
   if (grid > tg.num_tiles) grid = tg.num_tiles;
   // Cooperative launch: the round-robin tile order needs all CTAs resident.
@@ -341,16 +324,11 @@ int launch_tile(const typename P::Params& p, const Geom& g, void* ws, size_t ws_
   tg.edge_global = g.edge_global; tg.seg = g.seg;
   tg.stage_bytes = stage_layout<P>(p, K, tg.off);
   const int64_t outb = (int64_t)kTileThreads * K * 4 * (P::kOutSlots + P::kScratch);
-  const int64_t budget = (int64_t)env_int("RLS_TILE_SMEM_KB", 112) * 1024;
-  const int forced = env_int("RLS_TILE_NS", 0);
+  const int64_t budget = 112 * 1024;  // leaves room for two CTAs per SM
   int ns = 0;
-  if (forced >= 2 && forced <= kMaxStages) {
-    ns = forced;
-  } else {
-    for (int c = kMaxStages; c >= 2 && !ns; --c)
-      if (c * (int64_t)tg.stage_bytes + outb <= budget) ns = c;
-    if (!ns) ns = 2;
-  }
+  for (int c = kMaxStages; c >= 2 && !ns; --c)
+    if (c * (int64_t)tg.stage_bytes + outb <= budget) ns = c;
+  if (!ns) ns = 2;
   if (ns * (int64_t)tg.stage_bytes + outb > 220 * 1024) return RLS_EUNSUPPORTED;
   tg.stages = ns;
   return launch_tile_k<P, K>(p, tg, ws, ws_bytes, s);
@@ -368,10 +346,15 @@ struct TileL {
 template <class P>
 struct Rows2L {
   static int run(const typename P::Params& p, const Geom& g, void*, size_t, cudaStream_t s) {
-    const int forced = env_int("RLS_ROWS2_R", 0);
-    const int r = forced ? forced : 1;  // one round per chunk: the leanest registers measured fastest
+    // Rows of one chunk: the loop-free kernel, 8 rows per CTA (4 for the
+    // two-output policies, whose registers limit the resident CTAs); longer
+    // rows: one round per chunk (the leanest registers measured fastest).
+    constexpr int64_t kChunk = 32 * (16 / (int)sizeof(typename P::InT));
+    if (g.S <= kChunk) {
+      constexpr int W = P::kOuts > 1 ? 4 : 8;
+      return launch_rowk(rows1_kernel<P, W>, (g.N + W - 1) / W, W * 32, s, g, p.out0, p.out1, p, g);
+    }
     const int64_t blocks = (g.N + 3) / 4;
-    if (r >= 2) return launch_rowk(rows2_kernel<P, 4, 2>, blocks, 128, s, g, p.out0, p.out1, p, g);
     return launch_rowk(rows2_kernel<P, 4, 1>, blocks, 128, s, g, p.out0, p.out1, p, g);
   }
 };

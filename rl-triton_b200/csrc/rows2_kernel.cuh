@@ -232,10 +232,13 @@ struct ChunkScan {
 };
 
 // Scan one chunk of one row with the carry entering it; returns the carry leaving it.
+// wait_before_emit: the first chunk of a kernel launched with programmatic
+// stream serialization whose loads could start early (Geom::pdl == 2) waits
+// for the preceding grid only between its scan and its first store.
 template <class P, int R>
 __device__ __forceinline__ float rows2_chunk(const typename P::Params& p, const Geom& g, int64_t row,
                                              int64_t rbase, int64_t cbase, int lane, const Rows2Chunk<P, R>& ch,
-                                             float carry, typename P::Nbr& edge_nbr) {
+                                             float carry, typename P::Nbr& edge_nbr, bool wait_before_emit = false) {
   constexpr int VEC = Rows2Chunk<P, R>::VEC;
   constexpr bool BWD = P::kBackward;
   ChunkScan<P, R> cs;
@@ -248,11 +251,12 @@ __device__ __forceinline__ float rows2_chunk(const typename P::Params& p, const 
     cs.edge_v[r] = cs.valid[r] && (BWD ? (cs.col0[r] + VEC == g.S) : (cs.col0[r] == 0));
   }
   edge_nbr = cs.pass1(p, g, lane, ch, edge_nbr);
+  if (wait_before_emit) pdl_wait();
   return cs.pass2(p, g, ch, carry);
 }
 
-template <class P, int WPB, int R>
-__global__ void __launch_bounds__(WPB * 32) rows2_kernel(const typename P::Params p, const Geom g) {
+template <class P, int WPB, int R, int MINB = 1>
+__global__ void __launch_bounds__(WPB * 32, MINB) rows2_kernel(const typename P::Params p, const Geom g) {
   constexpr int VEC = Rows2Chunk<P, R>::VEC;
   constexpr int64_t CH = (int64_t)R * 32 * VEC;
   constexpr bool BWD = P::kBackward;
@@ -270,14 +274,38 @@ __global__ void __launch_bounds__(WPB * 32) rows2_kernel(const typename P::Param
   pdl_trigger();
   if (g.pdl == 1) pdl_wait();
   rows2_load<P, R>(p, rbase, S, cb_of(0), lane, a);
-  if (g.pdl == 2) pdl_wait();  // the first chunk's loads are in flight; no store before this
   for (int64_t k = 0; k < nch; k += 2) {
     if (k + 1 < nch) rows2_load<P, R>(p, rbase, S, cb_of(k + 1), lane, b);
-    carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k), lane, a, carry, edge_nbr);
+    // pdl == 2: the first chunk is loaded and scanned before the wait; no store precedes it
+    carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k), lane, a, carry, edge_nbr, g.pdl == 2 && k == 0);
     if (k + 1 >= nch) break;
     if (k + 2 < nch) rows2_load<P, R>(p, rbase, S, cb_of(k + 2), lane, a);
     carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k + 1), lane, b, carry, edge_nbr);
   }
+}
+
+// Rows of at most one chunk (seq_len <= 32 lanes x VEC, e.g. 4096 x 128 fp32):
+// one warp per row, WPB rows per CTA, no loop.  Launched with programmatic
+// stream serialization, such a kernel is short enough that the time between
+// two launches matters: it loads and scans its row before griddepcontrol.wait
+// (when its inputs are not the preceding launch's outputs, Geom::pdl == 2) and
+// only emits and stores after it.
+template <class P, int WPB>
+__global__ void __launch_bounds__(WPB * 32) rows1_kernel(const typename P::Params p, const Geom g) {
+  constexpr int VEC = Rows2Chunk<P, 1>::VEC;
+  constexpr bool BWD = P::kBackward;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * WPB + (threadIdx.x >> 5);
+  if (row >= g.N) return;  // whole warp exits together
+  const int64_t S = g.S;
+  pdl_trigger();
+  if (g.pdl == 1) pdl_wait();
+  Rows2Chunk<P, 1> ch;
+  rows2_load<P, 1>(p, row * S, S, 0, lane, ch);
+  typename P::Nbr edge_nbr{};
+  rows2_chunk<P, 1>(p, g, row, row * S, 0, lane, ch, 0.f, edge_nbr, g.pdl == 2);
+  (void)VEC;
+  (void)BWD;
 }
 
 }  // namespace rls
@@ -564,8 +592,8 @@ __device__ __forceinline__ void flat_chunk_setup(const Geom& g, int64_t cbase, i
   }
 }
 
-template <class P, int NCH, int R>
-__global__ void __launch_bounds__(128) flat3_kernel(const typename P::Params p, const Geom g, void* ws_base) {
+template <class P, int NCH, int R, int MINB = 1>
+__global__ void __launch_bounds__(128, MINB) flat3_kernel(const typename P::Params p, const Geom g, void* ws_base) {
   using CS = ChunkScan<P, R>;
   constexpr int RE = P::kBackward ? R - 1 : 0;  // round holding the entry element
   constexpr int VEC = CS::VEC;

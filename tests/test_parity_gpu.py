@@ -33,7 +33,7 @@ def T(a, dev="cuda", dtype=torch.float32):
     return torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)
 
 
-@pytest.fixture(autouse=True, params=["auto", "rows2", "vrows", "flat3", "flat2", "tile", "rows", "flat"])
+@pytest.fixture(autouse=True, params=["auto", "rows2", "vrows", "flat4", "flat3", "flat2", "tile", "rows", "flat"])
 def kernel_path(request, monkeypatch):
     """Run every case on each kernel family: the library's own choice ("auto"),
     the TMA-staged tile kernel, the row-parallel register kernel (one warp per
