@@ -283,6 +283,29 @@ def read_traffic(fn: str, workload: str):
     return None
 
 
+def read_write_peaks(dev):
+    """Context for fractions above 1.0: this GPU's read-only (sum over 4 GiB)
+    and write-only (fill of 4 GiB) HBM bandwidth, best of 5, CUDA events.  The
+    roofline denominator stays the driver-measured copy bandwidth."""
+    x = torch.empty(1 << 30, dtype=torch.float32, device=dev)
+    x.fill_(1.0)
+    res = {}
+    for name, fn in (("read_only_gbs", lambda: x.sum()), ("write_only_gbs", lambda: x.fill_(2.0))):
+        fn()
+        best = 1e9
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            best = min(best, e0.elapsed_time(e1))
+        res[name] = round(x.numel() * 4 / (best * 1e-3) / 1e9, 1)
+    del x
+    torch.cuda.empty_cache()
+    return res
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -422,10 +445,12 @@ def run_reference(args, world, rank):
 
 
 # --------------------------------------------------------------------------
-def time_function(calls, fname, stream, use_graph, min_reps=8, max_reps=200, budget_s=0.5, fixed_reps=0):
+def time_function(calls, fname, stream, use_graph, min_reps=8, max_reps=1000, budget_s=0.5, fixed_reps=0):
     """Device time per launch of one public call (CUDA graph of `reps` calls over
     the rotating input sets, CUDA events on the launching stream) and the eager
-    full-call time (the same calls issued from Python, device-resident inputs)."""
+    full-call time (the same calls issued from Python, device-resident inputs).
+    Up to 1000 launches per timing: outputs written back from L2 after the
+    timed region (at most the 126 MB L2) are then a small share of the bytes."""
     n_sets = len(calls)
     with torch.cuda.stream(stream):
         t0 = time.perf_counter()
@@ -732,18 +757,16 @@ def run_e2e(cfg, x0, dev, split, world, ksteps):
                     "every output; copies in / calls / copies out on three streams, two buffer sets"}
 
 
-def run_b200(args, world, rank, local):
-    cfg = CONFIGS[args.config]
-    split = world > 1 and cfg.get("split", False)
-    if split:  # strong scaling: each rank holds T / world columns of the one sequence
-        cfg = dict(cfg, T=cfg["T"] // world)
+def measure_step(cfg, split, world, rank, local, steps, warmup, no_graph=False, sets_override=0):
+    """Time `steps` steps of a workload (each step = one call of each of its
+    functions on one input set, replayed from a CUDA graph per input set)
+    between a barrier + synchronize on both sides; CUDA events on the launching
+    stream, max over ranks.  Returns the timing and what the later legs reuse."""
     dev = torch.device("cuda", local)
-    from rl_triton import _native as nat
-
     N, T = cfg["N"], cfg["T"]
     n_sets, per_set = input_sets(cfg)
-    if args.sets:
-        n_sets = args.sets
+    if sets_override:
+        n_sets = sets_override
     sets = [make_inputs(cfg, dev, seed=1000 * rank + k) for k in range(n_sets)]
     calls = [make_calls(cfg, x, split) for x in sets]
     stream = torch.cuda.Stream(dev)
@@ -755,7 +778,9 @@ def run_b200(args, world, rank, local):
                 f()
     stream.synchronize()
 
-    use_graph = not args.no_graph and not split  # the split path's collectives run eagerly
+    # The time-split path passes t0 / total, so it never synchronises the host
+    # and its collective is captured with the kernels.
+    use_graph = not no_graph
     graphs = []
     if use_graph:
         for c in calls:
@@ -775,7 +800,7 @@ def run_b200(args, world, rank, local):
     sampler = ClockSampler(local)
     sampler.start()
     with torch.cuda.stream(stream):
-        for k in range(args.warmup):
+        for k in range(warmup):
             step(k)
     stream.synchronize()
     barrier(world)
@@ -784,7 +809,7 @@ def run_b200(args, world, rank, local):
     tw0 = time.perf_counter()
     with torch.cuda.stream(stream):
         ev0.record(stream)
-        for k in range(args.steps):
+        for k in range(steps):
             step(k)
         ev1.record(stream)
     stream.synchronize()
@@ -793,11 +818,53 @@ def run_b200(args, world, rank, local):
     clocks = sampler.summary(tw0, tw1)
     barrier(world)
     torch.cuda.synchronize(dev)
-    ms_total = ev0.elapsed_time(ev1)
-    ms_total = max_over_ranks(ms_total, world)
-    ms = ms_total / args.steps
-    value = world * N * T / (ms / 1e3)
+    ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
+    ms = ms_total / steps
     graphs.clear()
+    return {"value": world * N * T / (ms / 1e3), "ms": ms, "sets": sets, "calls": calls, "stream": stream,
+            "use_graph": use_graph, "clocks": clocks, "n_sets": n_sets, "per_set": per_set}
+
+
+def run_sharded(args, world, rank, local):
+    """The two multi-GPU partitions in the same run as the headline line:
+    config 4 sharded along num_envs (weak: every rank its own 131072 x 1024) and
+    config 5b split along time (strong: one 2^28-step sequence cut into W
+    segments, one all-gather per call)."""
+    out = {}
+    for name in ("cfg4", "cfg5b"):
+        cfg = CONFIGS[name]
+        split = cfg.get("split", False) and world > 1
+        if split:
+            cfg = dict(cfg, T=cfg["T"] // world)
+        try:
+            m = measure_step(cfg, split, world, rank, local, max(3, min(args.steps, 20)), 3, args.no_graph)
+            out[name] = {"workload": CONFIGS[name]["desc"], "value": m["value"], "unit": "timesteps/s",
+                         "ms_per_step": m["ms"], "scaling": "strong" if name == "cfg5b" else "weak",
+                         "partition": ("time-split" if split else "single GPU") if name == "cfg5b"
+                         else ("env-sharded" if world > 1 else "single GPU"),
+                         "num_envs_per_gpu": cfg["N"], "seq_len_per_gpu": cfg["T"],
+                         "launch": "CUDA graph per input set" if m["use_graph"] else "eager",
+                         "clocks": m["clocks"]}
+            del m
+        except Exception as e:  # noqa: BLE001
+            out[name] = {"error": f"{type(e).__name__}: {str(e)[:300]}"}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_b200(args, world, rank, local):
+    cfg = CONFIGS[args.config]
+    split = world > 1 and cfg.get("split", False)
+    if split:  # strong scaling: each rank holds T / world columns of the one sequence
+        cfg = dict(cfg, T=cfg["T"] // world)
+    dev = torch.device("cuda", local)
+    from rl_triton import _native as nat
+
+    N, T = cfg["N"], cfg["T"]
+    m = measure_step(cfg, split, world, rank, local, args.steps, args.warmup, args.no_graph, args.sets)
+    value, ms, sets, calls, stream, use_graph = m["value"], m["ms"], m["sets"], m["calls"], m["stream"], m["use_graph"]
+    clocks, n_sets, per_set = m["clocks"], m["n_sets"], m["per_set"]
 
     # Per-function device time per launch and eager full-call time.
     per_fn = {}
@@ -809,6 +876,7 @@ def run_b200(args, world, rank, local):
         per_fn[fname] = {"us_per_launch": us, "full_call_us": t["full_call_us"], "algorithmic_bytes": alg,
                          "achieved_gbs": round(alg / (us * 1e-6) / 1e9, 1),
                          "frac": round(alg / (us * 1e-6) / 1e9 / hbm, 4)}
+    rw = read_write_peaks(dev) if rank == 0 else None
     dom = max(per_fn, key=lambda f: per_fn[f]["us_per_launch"])
     d = per_fn[dom]
     traffic = read_traffic(dom, args.config)
@@ -826,6 +894,10 @@ def run_b200(args, world, rank, local):
                 for key, t in flat_outputs(f, c()).items():
                     ours[key] = t[:rows, :cols].float().cpu().numpy()
         tri = triton_reference(args, cfg, ours, per_fn, local)
+
+    sharded = None
+    if not args.no_sharded and args.config == "cfg2":
+        sharded = run_sharded(args, world, rank, local)
 
     e2e = None
     if not args.no_e2e:
@@ -851,12 +923,14 @@ def run_b200(args, world, rank, local):
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": d["achieved_gbs"], "peak": hbm,
                          "unit": "GB/s", "frac": d["frac"], "traffic": traffic,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6650 GB/s"},
+                         else "fallback 6650 GB/s",
+                         "context": rw},
             "per_function": per_fn,
             "parity": parity,
             "triton_reference": tri,
             "clocks": clocks,
             "e2e": e2e,
+            "sharded": sharded,
             "cpu_baseline": cpu,
             "gpu_launches": n_launch,
             "lib": nat.build_info(),
@@ -936,6 +1010,8 @@ def main():
     ap.add_argument("--len", type=int, default=0, help="--ncu mode: override the sequence length T")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed outputs")
     ap.add_argument("--no-triton", action="store_true", help="skip timing the reference's Triton kernels")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the config 4 (env-sharded) and 5b (time-split) legs of the default run")
     ap.add_argument("--triton-worker", action="store_true", help=argparse.SUPPRESS)
     ap.add_argument("--device", type=int, default=0, help=argparse.SUPPRESS)
     ap.add_argument("--triton-out", default="", help=argparse.SUPPRESS)

@@ -196,11 +196,40 @@ int rls_segment_reduce(int alg, const void* flag0, const void* flag1, int in_dty
 /* Apply the true incoming carry (fp32 [N]) of each row to a segment's local
  * result: out[t] += P[t] * carry, P[t] = product of b over [t, edge].  Stops
  * at the first zero of P, so the work is bounded by the distance to the first
- * episode reset (or to underflow of the decay product).                     */
+ * episode reset (or to underflow of the decay product).
+ * With flags & RLS_SEG_EXCLUSIVE the carry is the correction entering at the
+ * segment's entry element itself, as rls_segment_compose returns it: for
+ * backward algorithms P leaves out the entry element's own decay
+ * (P[last] = 1), and a NULL halo reads as 0.                                */
+#define RLS_SEG_EXCLUSIVE 2
 int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtype,
                       float* out, const float* carry,
                       int64_t num_envs, int64_t seq_len, float coef, int flags,
                       const rls_segment_t* seg, void* stream);
+
+/* One-exchange time split.  Each rank scans its segment with the cut as
+ * carry 0 and a zero halo (no value from a neighbour is needed before the
+ * scan), then summarises every row in summary[5][N] (fp32):
+ *   0: A, the local state at the far edge (column 0 backward, S-1 forward);
+ *   1: B, the decay product from the entry element to the far edge (backward:
+ *      without the entry element's own decay);
+ *   2: backward: alpha, the weight the next segment's first value V carries in
+ *      the entry element (GAE: gamma*(1-term[S-1]) where trunc[S-1] == 0, else
+ *      0); forward: m, the next segment's entry gate taken from this segment's
+ *      last flag (1 - done[S-1] when the gate reads done[t-1], else 1);
+ *   3: backward: beta, the entry element's own decay b[S-1]; forward: 0;
+ *   4: backward GAE: V[0] of this segment; else 0.
+ * `values` is read by GAE only (may be NULL otherwise); gamma is GAE's
+ * discount; coef and flags as for rls_segment_reduce.  The ranks all-gather
+ * their summaries (20 bytes per row per rank, one collective), and
+ * rls_segment_compose turns the W summaries ([W][5][N], rank order) into the
+ * correction entering `rank`'s segment, which rls_segment_fixup applies with
+ * RLS_SEG_EXCLUSIVE.                                                         */
+int rls_segment_summary(int alg, const void* flag0, const void* flag1, const void* values, int in_dtype,
+                        const float* out, float* summary, int64_t num_envs, int64_t seq_len, float gamma,
+                        float coef, int flags, const rls_segment_t* seg, void* stream);
+int rls_segment_compose(const float* summaries, int rank, int world, int backward, int64_t num_envs,
+                        float* carry, void* stream);
 
 /* ---- GAE for callers that cannot allocate --------------------------------
  * No counterpart in the reference (its Triton path always allocates through

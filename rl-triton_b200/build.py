@@ -86,20 +86,53 @@ def build_torch_ops(force: bool = False) -> str:
     return TORCH_LIB
 
 
+OBJDIR = os.path.join(HERE, "_build")
+
+
+def _deps(src: str) -> list[str]:
+    # every source includes some of the headers; rebuild on any of them
+    return [os.path.join(CSRC, src)] + [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include",
+                                                                                               "rlscan.h")]
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile each csrc/*.cu to an object (in parallel, skipping objects newer
+    than their sources and headers), link librlscan.so, then the operator
+    library."""
     if not force and not _stale():
         build_torch_ops()
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
+    os.makedirs(OBJDIR, exist_ok=True)
+    procs = []
+    objs = []
+    for src in SOURCES:
+        obj = os.path.join(OBJDIR, src.replace(".cu", ".o"))
+        objs.append(obj)
+        if (not verbose and os.path.exists(obj)
+                and all(os.path.getmtime(obj) > os.path.getmtime(d) for d in _deps(src))):
+            continue
+        cmd = [nvcc_path(), *nvcc_flags(verbose), "-c", os.path.join(CSRC, src), "-o", obj + ".tmp"]
+        procs.append((obj, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)))
+    failed = False
+    for obj, pr in procs:
+        out, err = pr.communicate()
+        if pr.returncode != 0:
+            sys.stderr.write(out + err)
+            failed = True
+        else:
+            if verbose:
+                sys.stderr.write(err)
+            os.replace(obj + ".tmp", obj)
+    if failed:
+        raise RuntimeError("nvcc failed building librlscan.so")
     tmp = LIB + ".tmp"
-    cmd = [nvcc_path(), *nvcc_flags(verbose), "-shared", "-Xlinker", "-soname=librlscan.so", "-o", tmp]
-    cmd += [os.path.join(CSRC, f) for f in SOURCES]
+    cmd = [nvcc_path(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xlinker", "-soname=librlscan.so",
+           "-o", tmp, *objs]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building librlscan.so")
-    if verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError("nvcc failed linking librlscan.so")
     os.replace(tmp, LIB)
     build_torch_ops(force=True)
     return LIB

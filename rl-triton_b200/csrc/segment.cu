@@ -39,6 +39,10 @@ struct SegArgs {
   const float* halo;
   int global_edge;      // the segment holds the global row edge where the carry would enter
   int backward;
+  int exclusive;        // the entry element's own decay is left out of P (backward summaries)
+  const void* values;   // summary (GAE): V at the segment's first column
+  float gamma;          // summary (GAE): discount of the entry element's next value
+  float* summary;       // summary: [5][N]
 };
 
 __device__ __forceinline__ float load_in(const void* p, int bf16, int64_t i) {
@@ -61,7 +65,7 @@ __device__ float decay_at(const SegArgs& a, int64_t row, int64_t col) {
     case RLS_ALG_PREFIX: {
       const bool prev = (a.alg == RLS_ALG_ELIGIBILITY) || a.ends_at;
       float flag;
-      if (prev) flag = (col == 0) ? a.halo[row] : load_in(a.f0, a.bf16, i - 1);
+      if (prev) flag = (col == 0) ? (a.halo ? a.halo[row] : 0.f) : load_in(a.f0, a.bf16, i - 1);
       else flag = load_in(a.f0, a.bf16, i);
       const float k = (a.alg == RLS_ALG_ELIGIBILITY) ? a.coef : 1.f;
       return k * (1.f - flag);
@@ -71,7 +75,39 @@ __device__ float decay_at(const SegArgs& a, int64_t row, int64_t col) {
   }
 }
 
-// mode 0: reduce (seg_a, seg_b); mode 1: fix-up with carry.
+// Summary fields 2-4 of a row (fields 0-1, A and B, are the reduce's seg_a /
+// seg_b, which point into the same [5][N] buffer):
+//   backward: 2 = alpha, the weight of the next segment's first value V in the
+//             entry element (GAE: gamma (1 - term) where not truncated, else 0),
+//             3 = beta, the entry element's own decay b, 4 = V at column 0
+//             (GAE; 0 otherwise);
+//   forward:  2 = m, the factor the next segment's entry gate takes from this
+//             segment's last flag (1 - done[last] when the gate reads done[t-1],
+//             else 1); 3, 4 = 0.
+__device__ void write_summary(const SegArgs& a, int64_t row) {
+  const int64_t N = a.N, S = a.S;
+  float f2 = 0.f, f3 = 0.f, f4 = 0.f;
+  if (S > 0) {
+    const int64_t last = row * S + S - 1;
+    if (a.backward) {
+      f3 = decay_at(a, row, S - 1);
+      if (a.alg == RLS_ALG_GAE) {
+        const float term = load_in(a.f0, a.bf16, last);
+        const float trunc = a.f1 ? load_in(a.f1, a.bf16, last) : 0.f;
+        f2 = trunc == 0.f ? a.gamma * (1.f - term) : 0.f;
+        f4 = load_in(a.values, a.bf16, row * S);
+      }
+    } else {
+      const bool prev = (a.alg == RLS_ALG_ELIGIBILITY) || (a.alg == RLS_ALG_PREFIX && a.ends_at);
+      f2 = prev ? 1.f - load_in(a.f0, a.bf16, last) : 1.f;
+    }
+  }
+  a.summary[2 * N + row] = f2;
+  a.summary[3 * N + row] = f3;
+  a.summary[4 * N + row] = f4;
+}
+
+// mode 0: reduce (seg_a, seg_b) [+ summary]; mode 1: fix-up with carry.
 template <int MODE>
 __global__ void __launch_bounds__(128) segment_walk(const SegArgs a) {
   const int lane = threadIdx.x & 31;
@@ -91,7 +127,7 @@ __global__ void __launch_bounds__(128) segment_walk(const SegArgs a) {
     int64_t col = 0;
     if (k < S) {
       col = a.backward ? (S - 1 - k) : k;
-      b = decay_at(a, row, col);
+      b = (a.exclusive && k == 0) ? 1.f : decay_at(a, row, col);
     }
     // inclusive product scan over lanes in walk order
     float incl = b;
@@ -112,6 +148,7 @@ __global__ void __launch_bounds__(128) segment_walk(const SegArgs a) {
     const int64_t far = a.backward ? 0 : (S - 1);
     a.seg_a[row] = S > 0 ? a.out[row * S + far] : 0.f;
     a.seg_b[row] = zero ? 0.f : P;
+    if (a.summary) write_summary(a, row);
   }
 }
 
@@ -143,7 +180,7 @@ __global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a
     for (int q = 0; q < kBlockElems; ++q) {
       const int64_t k = k0 + (int64_t)threadIdx.x * kBlockElems + q;
       col[q] = k < S ? (a.backward ? (S - 1 - k) : k) : -1;
-      b[q] = col[q] >= 0 ? decay_at(a, row, col[q]) : 1.f;
+      b[q] = col[q] >= 0 ? ((a.exclusive && k == 0) ? 1.f : decay_at(a, row, col[q])) : 1.f;
     }
     float mine = 1.f;
 #pragma unroll
@@ -183,6 +220,7 @@ __global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a
     const int64_t far = a.backward ? 0 : (S - 1);
     a.seg_a[row] = S > 0 ? a.out[row * S + far] : 0.f;
     a.seg_b[row] = zero ? 0.f : base;
+    if (a.summary) write_summary(a, row);
   }
 }
 
@@ -196,7 +234,7 @@ int launch_walk(const SegArgs& a, void* stream) {
 }
 
 int fill_args(int alg, const void* flag0, const void* flag1, int in_dtype, int64_t N, int64_t S, float coef,
-              int flags, const rls_segment_t* seg, SegArgs& a) {
+              int flags, const rls_segment_t* seg, SegArgs& a, bool null_halo_is_zero = false) {
   if (alg < RLS_ALG_GAE || alg > RLS_ALG_SCAN_FWD || !flag0 || !seg || N < 0 || S < 0) return RLS_EINVAL;
   if (in_dtype != RLS_F32 && in_dtype != RLS_BF16) return RLS_EINVAL;
   if ((alg == RLS_ALG_SCAN_BWD || alg == RLS_ALG_SCAN_FWD) && in_dtype != RLS_F32) return RLS_EINVAL;
@@ -212,7 +250,11 @@ int fill_args(int alg, const void* flag0, const void* flag1, int in_dtype, int64
   a.backward = !(alg == RLS_ALG_ELIGIBILITY || alg == RLS_ALG_PREFIX || alg == RLS_ALG_SCAN_FWD);
   a.global_edge = a.backward ? (seg->t0 + S == seg->total_len) : (seg->t0 == 0);
   const bool needs_halo = (alg == RLS_ALG_ELIGIBILITY) || (alg == RLS_ALG_PREFIX && a.ends_at);
-  if (needs_halo && !a.halo && !a.global_edge) return RLS_EINVAL;
+  if (needs_halo && !a.halo && !a.global_edge && !null_halo_is_zero) return RLS_EINVAL;
+  a.exclusive = (flags & RLS_SEG_EXCLUSIVE) && a.backward;
+  a.values = nullptr;
+  a.gamma = 0.f;
+  a.summary = nullptr;
   return RLS_OK;
 }
 
@@ -435,7 +477,8 @@ int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtyp
                       int64_t num_envs, int64_t seq_len, float coef, int flags, const rls_segment_t* seg,
                       void* stream) {
   SegArgs a;
-  int st = fill_args(alg, flag0, flag1, in_dtype, num_envs, seq_len, coef, flags, seg, a);
+  int st = fill_args(alg, flag0, flag1, in_dtype, num_envs, seq_len, coef, flags, seg, a,
+                     (flags & RLS_SEG_EXCLUSIVE) != 0);
   if (st) return st;
   if (!out || !carry) return RLS_EINVAL;
   DeviceGuard guard{flag0, flag1, out, carry, seg ? seg->halo : nullptr};
@@ -448,4 +491,60 @@ int rls_segment_fixup(int alg, const void* flag0, const void* flag1, int in_dtyp
   return launch_walk<1>(a, stream);
 }
 
+int rls_segment_summary(int alg, const void* flag0, const void* flag1, const void* values, int in_dtype,
+                        const float* out, float* summary, int64_t num_envs, int64_t seq_len, float gamma,
+                        float coef, int flags, const rls_segment_t* seg, void* stream) {
+  SegArgs a;
+  int st = fill_args(alg, flag0, flag1, in_dtype, num_envs, seq_len, coef, flags | RLS_SEG_EXCLUSIVE, seg, a, true);
+  if (st) return st;
+  if (!out || !summary || (alg == RLS_ALG_GAE && !values)) return RLS_EINVAL;
+  DeviceGuard guard{flag0, flag1, values, out, summary, seg ? seg->halo : nullptr};
+  if (guard.status()) return guard.status();
+  a.out = const_cast<float*>(out);
+  a.carry = nullptr;
+  a.summary = summary;
+  a.seg_a = summary;
+  a.seg_b = summary + num_envs;
+  a.values = values;
+  a.gamma = gamma;
+  if (num_envs == 0) return RLS_OK;
+  return launch_walk<0>(a, stream);
+}
+
 }  // extern "C"
+
+namespace {
+// One thread per row: the carry entering rank `rank`'s segment from the W
+// summaries ([W][5][N], rank order).
+__global__ void segment_compose(const float* sm, int rank, int world, int backward, int64_t N, float* carry) {
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= N) return;
+  auto F = [&](int k, int f) { return sm[((int64_t)k * 5 + f) * N + row]; };
+  float c = 0.f;
+  if (backward) {
+    if (rank < world - 1) {
+      float s0 = F(world - 1, 0);  // state at the first column of the last segment
+      for (int k = world - 2; k > rank; --k) {
+        const float corr = fmaf(F(k, 3), s0, F(k, 2) * F(k + 1, 4));
+        s0 = fmaf(F(k, 1), corr, F(k, 0));
+      }
+      c = fmaf(F(rank, 3), s0, F(rank, 2) * F(rank + 1, 4));
+    }
+  } else {
+    for (int k = 0; k < rank; ++k) c = F(k, 2) * fmaf(F(k, 1), c, F(k, 0));
+  }
+  carry[row] = c;
+}
+}  // namespace
+
+extern "C" int rls_segment_compose(const float* summaries, int rank, int world, int backward, int64_t num_envs,
+                                   float* carry, void* stream) {
+  if (!summaries || !carry || world < 1 || rank < 0 || rank >= world || num_envs < 0) return RLS_EINVAL;
+  if (num_envs == 0) return RLS_OK;
+  DeviceGuard guard{summaries, carry};
+  if (guard.status()) return guard.status();
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  segment_compose<<<(unsigned)((num_envs + 255) / 256), 256, 0, s>>>(summaries, rank, world, backward, num_envs,
+                                                                    carry);
+  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+}

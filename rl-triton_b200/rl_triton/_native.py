@@ -34,6 +34,7 @@ ALG_ELIGIBILITY = 3
 ALG_PREFIX = 4
 ALG_SCAN_BWD = 5
 ALG_SCAN_FWD = 6
+SEG_EXCLUSIVE = 2
 
 
 class Segment(ctypes.Structure):
@@ -129,6 +130,8 @@ _SIGS = {
     "rls_affine_scan": (_I, [_P, _P, _P, _I, _P, _I64, _I64, _SEG, _P, _SZ, _P]),
     "rls_segment_reduce": (_I, [_I, _P, _P, _I, _P, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
     "rls_segment_fixup": (_I, [_I, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
+    "rls_segment_summary": (_I, [_I, _P, _P, _P, _I, _P, _P, _I64, _I64, _F, _F, _I, _SEG, _P]),
+    "rls_segment_compose": (_I, [_P, _I, _I, _I, _I64, _P, _P]),
     "rls_gae_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _F, _F, _I, _SEG, _P]),
     "rls_gae_noalloc_error": (_I, [_P]),
 }

@@ -5,24 +5,25 @@ No counterpart in the reference, which runs every scan on one device
 [t0_k, t0_k + S_k) of every row (its *segment*), with t0 given by the ranks'
 order.  Each call:
 
-1. exchanges the segment lengths (unless the caller passes `t0` and `total`,
-   which spares a host synchronisation) and the one-column halos the recurrences
-   read across a cut: backward GAE needs the next segment's first value
-   V[t0+S]; the forward scans gated by done[t-1] need the previous segment's
-   last flag;
-2. scans its segment with the cut treated as carry 0 (one kernel launch);
-3. summarises each row as the affine map (A, B): state at the far edge =
-   A + B * carry entering at the near edge (rls_segment_reduce);
-4. all-gathers the W maps (8 bytes per row per rank) and composes the true
-   carry of its cut from the ranks beyond it;
-5. applies it with the bounded fix-up out[t] += P[t] * carry, which stops
+1. scans its segment with the cut treated as carry 0 and every value from
+   across the cut (the next segment's first V for backward GAE, the previous
+   segment's last flag for the forward scans gated by done[t-1]) read as 0
+   (one kernel launch);
+2. summarises each row in five numbers (rls_segment_summary): the local state
+   at the far edge, the decay product across the segment, and the weights with
+   which the neighbour's value and state enter the entry element;
+3. all-gathers the W summaries (20 bytes per row per rank: the only
+   collective) and composes the correction entering its own segment
+   (rls_segment_compose, one small kernel);
+4. applies it with the bounded fix-up out[t] += P[t] * correction, which stops
    where the decay product P reaches 0 (rls_segment_fixup).
 
-Nothing else crosses ranks, so the collectives are two tiny all-gathers.  The
-collective and the three per-segment primitives are injectable (`all_gather`,
-`kernels`): the default is torch.distributed and librlscan; the tests drive the
-same code with gloo ranks and a CPU stand-in for the kernels, and with threads
-sharing one GPU.
+Without `t0` and `total` a first all-gather exchanges the segment lengths (and
+reads them on the host); with them the call never synchronises the host, so it
+can be captured in a CUDA graph.  The collective and the per-segment
+primitives are injectable (`all_gather`, `kernels`): the default is
+torch.distributed and librlscan; the tests drive the same code with gloo ranks
+and a CPU stand-in for the kernels, and with threads sharing one GPU.
 """
 from __future__ import annotations
 
@@ -77,34 +78,51 @@ class CudaKernels:
         else:
             f0, f1 = x["dones"], None
         dt = nat.dtype_code(f0)
+        if f1 is not None and f1.dtype != f0.dtype:
+            f1 = f1.to(f0.dtype)
         return f0.contiguous(), (f1.contiguous() if f1 is not None else None), dt
 
-    def reduce(self, alg, x, out, seg: Segment, halo, p):
+    def summary(self, alg, x, out, seg: Segment, p):
         f0, f1, dt = self._flags(alg, x)
         n, s = out.shape
-        ab = torch.empty(2, n, dtype=torch.float32, device=out.device)
-        st = nat.lib.rls_segment_reduce(alg, f0.data_ptr(), nat.ptr(f1), dt, out.data_ptr(), ab[0].data_ptr(),
-                                        ab[1].data_ptr(), n, s, float(p["coef"]), int(p["flags"]),
-                                        seg.cstruct(halo), nat.stream_handle(out.device))
-        nat.check(st, "rls_segment_reduce")
-        return ab
+        vals = None
+        if alg == GAE:
+            vals = x["values"]
+            vals = (vals if vals.dtype == f0.dtype else vals.to(f0.dtype)).contiguous()
+        sm = torch.empty(5, n, dtype=torch.float32, device=out.device)
+        st = nat.lib.rls_segment_summary(alg, f0.data_ptr(), nat.ptr(f1), nat.ptr(vals), dt, out.data_ptr(),
+                                         sm.data_ptr(), n, s, float(p.get("gamma", 0.0)), float(p["coef"]),
+                                         int(p["flags"]), seg.cstruct(None), nat.stream_handle(out.device))
+        nat.check(st, "rls_segment_summary")
+        return sm
 
-    def fixup(self, alg, x, out, carry, seg: Segment, halo, p):
+    def compose(self, maps: torch.Tensor, rank: int, world: int, backward: bool, n: int):
+        maps = maps.contiguous()
+        carry = torch.empty(n, dtype=torch.float32, device=maps.device)
+        st = nat.lib.rls_segment_compose(maps.data_ptr(), rank, world, 1 if backward else 0, n, carry.data_ptr(),
+                                         nat.stream_handle(maps.device))
+        nat.check(st, "rls_segment_compose")
+        return carry
+
+    def fixup(self, alg, x, out, carry, seg: Segment, p):
         f0, f1, dt = self._flags(alg, x)
         n, s = out.shape
         st = nat.lib.rls_segment_fixup(alg, f0.data_ptr(), nat.ptr(f1), dt, out.data_ptr(), carry.data_ptr(), n, s,
-                                       float(p["coef"]), int(p["flags"]), seg.cstruct(halo),
+                                       float(p["coef"]), int(p["flags"]) | nat.SEG_EXCLUSIVE, seg.cstruct(None),
                                        nat.stream_handle(out.device))
         nat.check(st, "rls_segment_fixup")
 
 
-def torch_all_gather(group=None) -> Callable[[torch.Tensor], list]:
+def torch_all_gather(group=None) -> Callable[[torch.Tensor], torch.Tensor]:
+    """All-gather over torch.distributed into one [W, *shape] tensor."""
     import torch.distributed as dist
 
-    def gather(t: torch.Tensor) -> list:
-        parts = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
-        dist.all_gather(parts, t.contiguous(), group=group)
-        return parts
+    def gather(t: torch.Tensor) -> torch.Tensor:
+        t = t.contiguous()
+        w = dist.get_world_size(group)
+        out = torch.empty((w * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t, group=group)
+        return out.view((w,) + tuple(t.shape))
 
     return gather
 
@@ -113,6 +131,22 @@ def _rank_world(group):
     import torch.distributed as dist
 
     return dist.get_rank(group), dist.get_world_size(group)
+
+
+_zero_halos: dict = {}
+
+
+def _zero_halo(n: int, device) -> torch.Tensor:
+    """A cached [n] fp32 zero vector: the cut's neighbour values in step 1."""
+    key = (str(device), n)
+    z = _zero_halos.get(key)
+    if z is None:
+        z = _zero_halos[key] = torch.zeros(n, dtype=torch.float32, device=device)
+    return z
+
+
+def _stacked(parts) -> torch.Tensor:
+    return parts if torch.is_tensor(parts) else torch.stack(list(parts))
 
 
 def _run(alg, x: dict, p: dict, ref: torch.Tensor, group=None, all_gather=None, kernels=None, rank=None,
@@ -126,40 +160,23 @@ def _run(alg, x: dict, p: dict, ref: torch.Tensor, group=None, all_gather=None, 
     dev = ref.device
     backward = alg in _BACKWARD
 
-    # (1) segment lengths and halos in one gather: [length, edge column].
-    if alg == GAE:
-        edge = x["values"][:, 0].float()           # our first value: the previous rank's halo
-    elif alg == ELIGIBILITY or (alg == PREFIX and p["boundary"] == "ends_at"):
-        edge = x["dones"][:, -1].float()           # our last flag: the next rank's halo
-    else:
-        edge = torch.zeros(n, dtype=torch.float32, device=dev)
-    # The length travels as two fp32 words (s // 2^20, s % 2^20), each exact
-    # below 2^24, so any length up to 2^44 arrives unrounded.
-    hi, lo = divmod(int(s), 1 << 20)
-    meta = torch.cat([torch.tensor([float(hi), float(lo)], dtype=torch.float32, device=dev), edge])
-    metas = all_gather(meta)
     if t0 is None or total is None:  # learn the layout (reads the lengths on the host)
-        lengths = [int(m[0].item()) * (1 << 20) + int(m[1].item()) for m in metas]
+        lengths = [int(v) for v in _stacked(all_gather(torch.tensor([s], dtype=torch.int64, device=dev))).view(-1)]
         t0, total = sum(lengths[:rank]), sum(lengths)
     seg = Segment(rank, world, t0, s, total)
+    at_end, at_start = t0 + s == total, t0 == 0
     halo = None
-    if alg == GAE and rank + 1 < world:
-        halo = metas[rank + 1][2:].contiguous()
-    elif alg in (ELIGIBILITY, PREFIX) and rank > 0:
-        halo = metas[rank - 1][2:].contiguous()
+    if alg == GAE and not at_end:
+        halo = _zero_halo(n, dev)
+    elif (alg == ELIGIBILITY or (alg == PREFIX and p["boundary"] == "ends_at")) and not at_start:
+        halo = _zero_halo(n, dev)
 
-    # (2)-(3) local scan with a cut, then the segment's map.
-    out = kernels.scan(alg, x, seg, halo, p)
-    ab = kernels.reduce(alg, x, out, seg, halo, p)
-    # (4) every rank's map; compose the carry entering this segment.
-    maps = all_gather(ab)
-    carry = torch.zeros(n, dtype=torch.float32, device=dev)
-    order = range(world - 1, rank, -1) if backward else range(0, rank)
-    for j in order:
-        carry = maps[j][0] + maps[j][1] * carry
-    # (5) bounded fix-up (a no-op on the segment holding the global edge).
-    if (rank < world - 1) if backward else (rank > 0):
-        kernels.fixup(alg, x, out, carry, seg, halo, p)
+    out = kernels.scan(alg, x, seg, halo, p)                 # (1) local scan, cut as carry 0
+    summary = kernels.summary(alg, x, out, seg, p)           # (2) [5, n]
+    maps = _stacked(all_gather(summary))                     # (3) [W, 5, n]: the one collective
+    carry = kernels.compose(maps, rank, world, backward, n)
+    if not (at_end if backward else at_start):               # (4) bounded fix-up
+        kernels.fixup(alg, x, out, carry, seg, p)
     return out
 
 

@@ -1,5 +1,6 @@
-"""CPU stand-in for the three per-segment primitives of rl_triton.dist
-(local scan with a cut, segment map, bounded fix-up), built on the C oracle.
+"""CPU stand-in for the per-segment primitives of rl_triton.dist (local scan
+with a cut, segment summary, carry composition, bounded fix-up), built on the
+C oracle.
 Test infrastructure only: it lets gloo ranks on CPU drive the real
 time-split driver (halo exchange, carry composition, fix-up placement)."""
 from __future__ import annotations
@@ -67,22 +68,51 @@ class CpuKernels:
         # columns from the edge where the carry enters inward
         return alg in (D.GAE, D.LAMBDA, D.DISCOUNTED)
 
-    def _products(self, alg, x, p, halo):
+    def _products(self, alg, x, p, halo, exclusive):
         b = _decays(alg, x, p, halo)
         if self._walk(alg, p):
+            if exclusive:
+                b = b.copy()
+                b[:, -1] = 1.0  # the entry element's own decay is left out
             return np.flip(np.cumprod(np.flip(b, 1), axis=1, dtype=np.float32), 1)
         return np.cumprod(b, axis=1, dtype=np.float32)
 
-    def reduce(self, alg, x, out, seg, halo, p):
+    def summary(self, alg, x, out, seg, p):
         backward = self._walk(alg, p)
         global_edge = (seg.t0 + seg.length == seg.total) if backward else seg.t0 == 0
-        P = self._products(alg, x, p, halo)
-        far = 0 if backward else -1
-        a = out[:, far].numpy()
-        b = np.zeros_like(a) if global_edge else P[:, far]
-        return torch.from_numpy(np.stack([a, b]).astype(np.float32))
+        P = self._products(alg, x, p, None, True)
+        n = out.shape[0]
+        sm = np.zeros((5, n), np.float32)
+        sm[0] = out[:, 0 if backward else -1].numpy()
+        sm[1] = 0.0 if global_edge else P[:, 0 if backward else -1]
+        if backward:
+            sm[3] = _decays(alg, x, p, None)[:, -1]
+            if alg == D.GAE:
+                term = _np(x["terminateds"])[:, -1]
+                tr = _np(x["truncateds"])[:, -1] if x.get("truncateds") is not None else np.zeros(n, np.float32)
+                sm[2] = np.where(tr == 0, np.float32(p["gamma"]) * (1 - term), 0).astype(np.float32)
+                sm[4] = _np(x["values"])[:, 0]
+        else:
+            gate_prev = alg == D.ELIGIBILITY or p["boundary"] == "ends_at"
+            sm[2] = (1 - _np(x["dones"])[:, -1]) if gate_prev else 1.0
+        return torch.from_numpy(sm)
 
-    def fixup(self, alg, x, out, carry, seg, halo, p):
-        P = self._products(alg, x, p, halo)
+    def compose(self, maps, rank, world, backward, n):
+        m = maps.numpy().astype(np.float32)
+        if backward:
+            if rank == world - 1:
+                return torch.zeros(n)
+            s0 = m[world - 1, 0]
+            for k in range(world - 2, rank, -1):
+                corr = m[k, 2] * m[k + 1, 4] + m[k, 3] * s0
+                s0 = m[k, 0] + m[k, 1] * corr
+            return torch.from_numpy((m[rank, 2] * m[rank + 1, 4] + m[rank, 3] * s0).astype(np.float32))
+        c = np.zeros(n, np.float32)
+        for k in range(rank):
+            c = m[k, 2] * (m[k, 0] + m[k, 1] * c)
+        return torch.from_numpy(c.astype(np.float32))
+
+    def fixup(self, alg, x, out, carry, seg, p):
+        P = self._products(alg, x, p, None, True)
         o = out.numpy()
         o += P * carry.numpy()[:, None]
