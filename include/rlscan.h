@@ -28,7 +28,8 @@
  *    must belong to that GPU.
  *  - Return value: RLS_OK (0) or an RLS_E* status; rls_status_string() names
  *    it.  Launches are asynchronous; device-side failures (a bounded wait that
- *    ran out) are latched in the workspace and read with rls_workspace_error().
+ *    ran out) are latched in the workspace and read with rls_workspace_error()
+ *    (bits: 1 tile look-back, 2 bulk copy, 4 grid barrier).
  */
 #ifndef RLSCAN_H
 #define RLSCAN_H
@@ -174,6 +175,57 @@ int rls_prefix_sum(const void* inputs, const void* dones, const float* seed_valu
 int rls_affine_scan(const float* u, const float* v, const float* carry, int direction,
                     float* out, int64_t num_envs, int64_t seq_len,
                     const rls_segment_t* seg, void* ws, size_t ws_bytes, void* stream);
+
+/* ---- fused epilogues (no counterpart in the reference: its ROADMAP.md lists
+ * "fused GAE + advantage normalisation" for v0.2) ------------------------- */
+
+/* GAE with the advantages normalised over the whole batch, as a PPO update
+ * uses them:  A = GAE (arguments as rls_gae, no time split),
+ *   mean = sum(A) / M,  std = sqrt(sum((A - mean)^2) / (M - 1))  (M = N*T,
+ *   unbiased like torch.std),  normalized = (A - mean) / (std + eps).
+ * Optional outputs (NULL to skip): returns = A + V (the value targets), the
+ * raw advantages A, and stats = fp32[2] {mean, std}.  When the batch fits in
+ * shared memory across one wave of CTAs (e.g. 4096 x 128, 4096 x 1024) one
+ * cooperative kernel reads the inputs once and writes the outputs once;
+ * larger batches take GAE, a statistics pass and a normalise pass.  The
+ * workspace (as for rls_gae) also holds the fp64 partial sums and a grid
+ * barrier counter.  Results are deterministic.                               */
+int rls_gae_normalized(const void* rewards, const void* values, const void* terminateds,
+                       const void* truncateds, const void* bootstrap, int boot_kind,
+                       float* normalized, float* returns, float* advantages, float* stats,
+                       int64_t num_envs, int64_t seq_len, float gamma, float lambda_, float eps,
+                       int in_dtype, void* ws, size_t ws_bytes, void* stream);
+
+/* GAE and the value loss of a PPO update in one pass.  For the value head's
+ * predictions V' (fp32 [N, T]):  A = GAE (arguments as rls_gae),
+ *   returns = A + V,  d = V' - returns,
+ *   loss = mean(d^2)  (RLS_LOSS_MSE, torch.nn.functional.mse_loss)  or
+ *          mean(|d| < delta ? d^2 / 2 : delta * (|d| - delta / 2))  (RLS_LOSS_HUBER,
+ *          torch.nn.functional.huber_loss),
+ * written to loss (fp32 scalar), and its gradient with respect to V' to grad
+ * (fp32 [N, T]) for the backward pass.  advantages and returns may be NULL.
+ * The per-CTA partial sums live in the workspace; deterministic.             */
+#define RLS_LOSS_MSE   0
+#define RLS_LOSS_HUBER 1
+int rls_gae_value_loss(const void* rewards, const void* values, const void* terminateds,
+                       const void* truncateds, const void* bootstrap, int boot_kind,
+                       const float* new_values, float* advantages, float* returns, float* grad,
+                       float* loss, int64_t num_envs, int64_t seq_len, float gamma, float lambda_,
+                       int loss_kind, float delta, int in_dtype, void* ws, size_t ws_bytes, void* stream);
+
+/* GAE with observation-skip masking for multi-turn / tool-use rollouts (the
+ * boundary mode the reference's ROADMAP.md lists for v0.2): tokens with
+ * mask 0 (observations) pass the recurrence through unchanged, and a
+ * generated token's TD error uses the value of the next generated token:
+ *   NV[t] = V of the next token after t with mask 1 (0 if none),
+ *   A[t]  = mask[t] ? r[t] + gamma*NV[t] - V[t] + gamma*lambda*A[t+1] : A[t+1],
+ *   A[T]  = 0.
+ * rewards, values and mask are [N, T] in in_dtype (mask in {0, 1});
+ * advantages (fp32) is required, returns = A + V (fp32) may be NULL.  One
+ * warp per row scans both recurrences chunk by chunk.  No workspace.         */
+int rls_gae_obs_skip(const void* rewards, const void* values, const void* mask, float* advantages,
+                     float* returns, int64_t num_envs, int64_t seq_len, float gamma, float lambda_,
+                     int in_dtype, void* stream);
 
 /* ---- time-split helpers (no counterpart in the reference, which has no
  * multi-GPU support; they implement the carry exchange of a sequence split

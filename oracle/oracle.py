@@ -50,6 +50,7 @@ _ARGS = {
     "orc_eligibility": [_P, _P, _P, _P, _I64, _I64, _D, _D],
     "orc_prefix": [_P, _P, _P, _I, _P, _I64, _I64],
     "orc_scan": [_P, _P, _P, _I, _P, _I64, _I64],
+    "orc_gae_obs_skip": [_P, _P, _P, _P, _P, _I64, _I64, _D, _D],
 }
 for _n, _a in _ARGS.items():
     for _s in ("_f32", "_f64"):
@@ -214,6 +215,22 @@ def affine_scan(u, v, carry=None, direction=0, precision="f32", nthreads=None):
 
     _rows(N, go, nthreads)
     return out
+
+
+def gae_obs_skip(r, v, mask, gamma=1.0, lam=1.0, precision="f32", nthreads=None):
+    """Observation-skip GAE (the boundary mode of the reference's ROADMAP.md
+    v0.2; no code counterpart there): returns (advantages, returns)."""
+    r, v, mask = map(_f32, (r, v, mask))
+    N, T = r.shape
+    adv, ret = _out((N, T), precision), _out((N, T), precision)
+    fn = getattr(_lib, "orc_gae_obs_skip_" + precision)
+
+    def go(n0, cnt):
+        o = n0 * T
+        fn(_p(r, o), _p(v, o), _p(mask, o), _p(adv, o), _p(ret, o), cnt, T, gamma, lam)
+
+    _rows(N, go, nthreads)
+    return adv, ret
 
 
 def compare(got, oracle, rtol=1e-5, atol=1e-5):

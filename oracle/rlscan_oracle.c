@@ -255,3 +255,29 @@ void FN(orc_scan)(const float* u, const float* v, const float* carry0, int direc
         }
     }
 }
+
+/*
+ * GAE with observation-skip masking.  No code counterpart in the reference:
+ * restates the boundary mode its ROADMAP.md (v0.2, "Multi-turn /
+ * observation-skip masking") describes -- masked tokens pass the recurrence
+ * through unchanged and the next valid token's TD error uses the pre-skip
+ * value.  Sequential loop: nextvalue and the running advantage are carried
+ * backward and only updated at tokens with mask 1.
+ */
+void FN(orc_gae_obs_skip)(const float* r, const float* v, const float* mask, REAL* adv, REAL* ret, int64_t N,
+                          int64_t T, double gamma_, double lam_) {
+    const REAL gamma = (REAL)(float)gamma_, gl = (REAL)((float)gamma_ * (float)lam_);
+    for (int64_t n = 0; n < N; ++n) {
+        REAL nextvalue = 0, running = 0;
+        for (int64_t t = T - 1; t >= 0; --t) {
+            const int64_t i = n * T + t;
+            if (mask[i] != 0) {
+                const REAL delta = (REAL)r[i] + gamma * nextvalue - (REAL)v[i];
+                running = delta + gl * running;
+                nextvalue = (REAL)v[i];
+            }
+            adv[i] = running;
+            ret[i] = running + (REAL)v[i];
+        }
+    }
+}

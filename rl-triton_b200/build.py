@@ -20,8 +20,8 @@ CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "rl_triton", "_lib")
 LIB = os.path.join(LIBDIR, "librlscan.so")
 TORCH_LIB = os.path.join(LIBDIR, "librlscan_torch.so")
-SOURCES = ["rlscan.cu", "segment.cu"]
-HEADERS = ["common.cuh", "algs.cuh", "scan_kernel.cuh", "rows_kernel.cuh", "rows2_kernel.cuh", "tile_kernel.cuh", "tile_policies.cuh"]
+SOURCES = ["rlscan.cu", "segment.cu", "ppo.cu"]
+HEADERS = ["common.cuh", "algs.cuh", "scan_kernel.cuh", "rows_kernel.cuh", "rows2_kernel.cuh", "tile_kernel.cuh", "tile_policies.cuh", "host_shared.h"]
 
 
 def nvcc_path() -> str:

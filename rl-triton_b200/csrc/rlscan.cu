@@ -16,24 +16,24 @@
 #include "rows_kernel.cuh"
 #include "tile_policies.cuh"
 #include "rows2_kernel.cuh"
+#include "host_shared.h"
 
 using namespace rls;
 
-namespace {
+namespace rls {
+std::recursive_mutex& launch_mutex() {
+  static std::recursive_mutex mu;
+  return mu;
+}
 
-constexpr int kWarps = 4;
-constexpr int64_t kMinTileElems = 128;  // smallest tile of any launch (a one-round fp32 flat2 tile)
-
-inline bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15u) == 0; }
-
-// Two record layouts share one workspace: the flags | aggregates | inclusive
-// layout of the flat look-back and tile kernels (ws_carve), and the packed
-// 64-bit value|tag words of flat2/3/4 (packed_carve).  A stale float left by
+// Record layouts share one workspace: the flags | aggregates | inclusive
+// layout of the flat look-back and tile kernels (ws_carve), the packed 64-bit
+// value|tag words of flat2/3/4 (packed_carve), and the fp64 partial sums of the
+// normalising GAE (ppo.cu).  A stale float left by
 // one layout could carry bits equal to a valid tag of the other, so the first
 // launch of a layout on a workspace last used by the other one clears the
 // records (the header, with the epoch, is kept).  Tracked per workspace
 // pointer on the host, under the launch lock.
-enum : int { kLayoutNone = 0, kLayoutFlags = 1, kLayoutPacked = 2 };
 int prepare_layout(void* ws, size_t wsb, int layout, cudaStream_t s) {
   static void* last_ws[64] = {nullptr};
   static int last_layout[64] = {0};
@@ -56,6 +56,14 @@ int prepare_layout(void* ws, size_t wsb, int layout, cudaStream_t s) {
   }
   return RLS_OK;
 }
+}  // namespace rls
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int64_t kMinTileElems = 128;  // smallest tile of any launch (a one-round fp32 flat2 tile)
+
+inline bool aligned16(const void* p) { return p == nullptr || ((uintptr_t)p & 15u) == 0; }
 
 // Rounds per warp: larger tiles for large inputs (fewer look-back hops, more
 // bytes in flight per thread); small inputs keep enough CTAs to fill 148 SMs.
@@ -681,10 +689,7 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 // and the epoch advance after it; the three virtual-row launches), and host
 // threads that share a stream must not interleave those sequences.  Only the
 // enqueue is serialised (microseconds), never the GPU work.
-std::recursive_mutex& launch_mutex() {
-  static std::recursive_mutex mu;
-  return mu;
-}
+
 
 bool valid_dtype(int d) { return d == RLS_F32 || d == RLS_BF16; }
 

@@ -189,8 +189,18 @@ struct ChunkScan {
   }
 
   // Emit and store with the carry entering the chunk; returns the carry leaving it.
+  // `sink(r, q, v0, v1)` takes the outputs of elements q..q+3 of round r
+  // (flat index i0[r] + q); the default streams them to out0 / out1.
   __device__ __forceinline__ float pass2(const typename P::Params& p, const Geom& g, const Chunk& ch,
                                          float carry) {
+    return pass2(p, g, ch, carry, [&](int r, int q, float4 v0, float4 v1) {
+      st_stream_f4(p.out0 + i0[r] + q, v0);
+      if constexpr (P::kOuts > 1) st_stream_f4(p.out1 + i0[r] + q, v1);
+    });
+  }
+  template <class Sink>
+  __device__ __forceinline__ float pass2(const typename P::Params& p, const Geom& g, const Chunk& ch,
+                                         float carry, Sink&& sink) {
     const int glob = g.edge_global;
     float cr[R];
     float c = carry;
@@ -221,9 +231,9 @@ struct ChunkScan {
       if (valid[r]) {
 #pragma unroll
         for (int q = 0; q < VEC; q += 4) {
-          st_stream_f4(p.out0 + i0[r] + q, make_float4(o0[q], o0[q + 1], o0[q + 2], o0[q + 3]));
-          if constexpr (P::kOuts > 1)
-            st_stream_f4(p.out1 + i0[r] + q, make_float4(o1[q], o1[q + 1], o1[q + 2], o1[q + 3]));
+          float4 v1 = make_float4(0.f, 0.f, 0.f, 0.f);
+          if constexpr (P::kOuts > 1) v1 = make_float4(o1[q], o1[q + 1], o1[q + 2], o1[q + 3]);
+          sink(r, q, make_float4(o0[q], o0[q + 1], o0[q + 2], o0[q + 3]), v1);
         }
       }
     }
@@ -323,7 +333,7 @@ namespace rls {
 // counter.
 // ===========================================================================
 
-__global__ void advance_epoch(void* ws_base) {
+static __global__ void advance_epoch(void* ws_base) {
   WsHeader* h = reinterpret_cast<WsHeader*>(ws_base);
   h->epoch = (h->epoch + 1u) & kEpochMask;
 }

@@ -124,6 +124,65 @@ Tensor op_gae(const Tensor& rewards, const Tensor& values, const Tensor& termina
   return out;
 }
 
+// (normalized advantages, returns = A + V)
+std::tuple<Tensor, Tensor> op_gae_normalized(const Tensor& rewards, const Tensor& values, const Tensor& terminateds,
+                                             const OptT& truncateds, const OptT& bootstrap, int64_t boot_kind,
+                                             double gamma, double lambda_, double eps) {
+  OptT r = rewards, v = values, term = terminateds, tr = truncateds;
+  OptT full = boot_kind == RLS_BOOT_ROW ? OptT() : bootstrap;
+  const int dt = unify({&r, &v, &term, &tr, &full});
+  r = ready(r); v = ready(v); term = ready(term); tr = ready(tr); full = ready(full);
+  OptT row = boot_kind == RLS_BOOT_ROW ? f32(bootstrap) : OptT();
+  const int64_t n = rewards.size(0), t = rewards.size(1);
+  Tensor norm = empty_f32(*r), rets = empty_f32(*r);
+  cudaStream_t s = stream_of(*r);
+  Tensor ws = workspace_for(r->device(), s, n * t < (1 << 20) ? (1 << 20) : n * t);
+  check(rls_gae_normalized(P(r), P(v), P(term), P(tr), boot_kind == RLS_BOOT_ROW ? P(row) : P(full), (int)boot_kind,
+                           norm.data_ptr<float>(), rets.data_ptr<float>(), nullptr, nullptr, n, t, (float)gamma,
+                           (float)lambda_, (float)eps, dt, ws.data_ptr(), (size_t)ws.numel(), s),
+        "rls_gae_normalized");
+  return {norm, rets};
+}
+
+// (advantages, returns, loss scalar, d loss / d new_values)
+std::tuple<Tensor, Tensor, Tensor, Tensor> op_gae_value_loss(const Tensor& rewards, const Tensor& values,
+                                                             const Tensor& terminateds, const OptT& truncateds,
+                                                             const OptT& bootstrap, int64_t boot_kind,
+                                                             const Tensor& new_values, double gamma, double lambda_,
+                                                             int64_t loss_kind, double delta) {
+  OptT r = rewards, v = values, term = terminateds, tr = truncateds;
+  OptT full = boot_kind == RLS_BOOT_ROW ? OptT() : bootstrap;
+  const int dt = unify({&r, &v, &term, &tr, &full});
+  r = ready(r); v = ready(v); term = ready(term); tr = ready(tr); full = ready(full);
+  OptT row = boot_kind == RLS_BOOT_ROW ? f32(bootstrap) : OptT();
+  const Tensor nv = f32(new_values);
+  const int64_t n = rewards.size(0), t = rewards.size(1);
+  Tensor adv = empty_f32(*r), rets = empty_f32(*r), grad = empty_f32(*r);
+  Tensor loss = at::empty({}, r->options().dtype(at::kFloat));
+  cudaStream_t s = stream_of(*r);
+  Tensor ws = workspace_for(r->device(), s, n * t < (1 << 20) ? (1 << 20) : n * t);
+  check(rls_gae_value_loss(P(r), P(v), P(term), P(tr), boot_kind == RLS_BOOT_ROW ? P(row) : P(full), (int)boot_kind,
+                           nv.data_ptr<float>(), adv.data_ptr<float>(), rets.data_ptr<float>(), grad.data_ptr<float>(),
+                           loss.data_ptr<float>(), n, t, (float)gamma, (float)lambda_, (int)loss_kind, (float)delta, dt,
+                           ws.data_ptr(), (size_t)ws.numel(), s),
+        "rls_gae_value_loss");
+  return {adv, rets, loss, grad};
+}
+
+// (advantages, returns) with observation-skip masking
+std::tuple<Tensor, Tensor> op_gae_obs_skip(const Tensor& rewards, const Tensor& values, const Tensor& mask,
+                                           double gamma, double lambda_) {
+  OptT r = rewards, v = values, m = mask;
+  const int dt = unify({&r, &v, &m});
+  r = ready(r); v = ready(v); m = ready(m);
+  const int64_t n = rewards.size(0), t = rewards.size(1);
+  Tensor adv = empty_f32(*r), rets = empty_f32(*r);
+  check(rls_gae_obs_skip(P(r), P(v), P(m), adv.data_ptr<float>(), rets.data_ptr<float>(), n, t, (float)gamma,
+                         (float)lambda_, dt, stream_of(*r)),
+        "rls_gae_obs_skip");
+  return {adv, rets};
+}
+
 std::tuple<Tensor, Tensor> op_vtrace(const Tensor& lpt, const Tensor& lpb, const Tensor& values,
                                      const Tensor& rewards, const Tensor& terminateds, const OptT& truncateds,
                                      const OptT& bootstrap, int64_t boot_kind, double gamma, double rho_bar,
@@ -270,6 +329,12 @@ int64_t op_workspace_error(const Tensor& like) {
 TORCH_LIBRARY(rl_triton, m) {
   m.def("gae(Tensor rewards, Tensor values, Tensor terminateds, Tensor? truncateds, Tensor? bootstrap, "
         "int boot_kind, float gamma, float lambda_, int t0=-1, int total=-1, Tensor? halo=None) -> Tensor");
+  m.def("gae_normalized(Tensor rewards, Tensor values, Tensor terminateds, Tensor? truncateds, Tensor? bootstrap, "
+        "int boot_kind, float gamma, float lambda_, float eps) -> (Tensor, Tensor)");
+  m.def("gae_value_loss(Tensor rewards, Tensor values, Tensor terminateds, Tensor? truncateds, Tensor? bootstrap, "
+        "int boot_kind, Tensor new_values, float gamma, float lambda_, int loss_kind, float delta) "
+        "-> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("gae_obs_skip(Tensor rewards, Tensor values, Tensor mask, float gamma, float lambda_) -> (Tensor, Tensor)");
   m.def("vtrace(Tensor log_pi_target, Tensor log_pi_behavior, Tensor values, Tensor rewards, Tensor terminateds, "
         "Tensor? truncateds, Tensor? bootstrap, int boot_kind, float gamma, float rho_bar, float c_bar) "
         "-> (Tensor, Tensor)");
@@ -293,6 +358,9 @@ TORCH_LIBRARY(rl_triton, m) {
 
 TORCH_LIBRARY_IMPL(rl_triton, CUDA, m) {
   m.impl("gae", &op_gae);
+  m.impl("gae_normalized", &op_gae_normalized);
+  m.impl("gae_value_loss", &op_gae_value_loss);
+  m.impl("gae_obs_skip", &op_gae_obs_skip);
   m.impl("vtrace", &op_vtrace);
   m.impl("retrace", &op_retrace);
   m.impl("lambda_returns", &op_lambda);

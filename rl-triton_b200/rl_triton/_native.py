@@ -35,6 +35,8 @@ ALG_PREFIX = 4
 ALG_SCAN_BWD = 5
 ALG_SCAN_FWD = 6
 SEG_EXCLUSIVE = 2
+LOSS_MSE = 0
+LOSS_HUBER = 1
 
 
 class Segment(ctypes.Structure):
@@ -71,6 +73,22 @@ def _f32_like(t):
 @torch.library.register_fake("rl_triton::gae")
 def _(rewards, values, terminateds, truncateds, bootstrap, boot_kind, gamma, lambda_, t0=-1, total=-1, halo=None):
     return _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::gae_normalized")
+def _(rewards, values, terminateds, truncateds, bootstrap, boot_kind, gamma, lambda_, eps):
+    return _f32_like(rewards), _f32_like(rewards)
+
+
+@torch.library.register_fake("rl_triton::gae_value_loss")
+def _(rewards, values, terminateds, truncateds, bootstrap, boot_kind, new_values, gamma, lambda_, loss_kind, delta):
+    return (_f32_like(rewards), _f32_like(rewards), torch.empty((), dtype=torch.float32, device=rewards.device),
+            _f32_like(rewards))
+
+
+@torch.library.register_fake("rl_triton::gae_obs_skip")
+def _(rewards, values, mask, gamma, lambda_):
+    return _f32_like(rewards), _f32_like(rewards)
 
 
 @torch.library.register_fake("rl_triton::vtrace")
@@ -132,6 +150,10 @@ _SIGS = {
     "rls_segment_fixup": (_I, [_I, _P, _P, _I, _P, _P, _I64, _I64, _F, _I, _SEG, _P]),
     "rls_segment_summary": (_I, [_I, _P, _P, _P, _I, _P, _P, _I64, _I64, _F, _F, _I, _SEG, _P]),
     "rls_segment_compose": (_I, [_P, _I, _I, _I, _I64, _P, _P]),
+    "rls_gae_normalized": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _I64, _I64, _F, _F, _F, _I, _P, _SZ, _P]),
+    "rls_gae_value_loss": (_I, [_P, _P, _P, _P, _P, _I, _P, _P, _P, _P, _P, _I64, _I64, _F, _F, _I, _F, _I, _P, _SZ,
+                                _P]),
+    "rls_gae_obs_skip": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _F, _F, _I, _P]),
     "rls_gae_noalloc": (_I, [_P, _P, _P, _P, _P, _I, _P, _I64, _I64, _F, _F, _I, _SEG, _P]),
     "rls_gae_noalloc_error": (_I, [_P]),
 }

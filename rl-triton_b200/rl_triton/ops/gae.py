@@ -41,6 +41,20 @@ def compute_gae(
     Returns:
         advantages: A[t], shape [num_envs, seq_len], float32.
     """
+    kind, boot = _gae_args(rewards, values, terminateds, truncateds, bootstrap_values, last_value)
+    _placed(rewards, values, terminateds, truncateds, boot, last_value)
+    _warn_copies({"rewards": rewards, "values": values, "terminateds": terminateds, "truncateds": truncateds,
+                  "bootstrap_values": boot})
+    t0, total, halo = _seg(_segment)
+    out = nat.ops.gae(rewards, values, terminateds, truncateds, last_value if kind == nat.BOOT_ROW else boot, kind,
+                      float(gamma), float(lambda_), t0, total, halo)
+    _done(rewards)
+    return out
+
+
+def _gae_args(rewards, values, terminateds, truncateds, bootstrap_values, last_value):
+    """The reference's argument checks (src/rl_triton/ops/gae.py:106-145) and
+    its bootstrap dispatch (:153-215); returns (boot_kind, bootstrap tensor)."""
     num_envs, seq_len = rewards.shape
     has_truncations = truncateds is not None
 
@@ -98,12 +112,4 @@ def compute_gae(
         boot = bootstrap_values
     else:
         kind = nat.BOOT_NONE
-
-    _placed(rewards, values, terminateds, truncateds, boot, last_value)
-    _warn_copies({"rewards": rewards, "values": values, "terminateds": terminateds, "truncateds": truncateds,
-                  "bootstrap_values": boot})
-    t0, total, halo = _seg(_segment)
-    out = nat.ops.gae(rewards, values, terminateds, truncateds, last_value if kind == nat.BOOT_ROW else boot, kind,
-                      float(gamma), float(lambda_), t0, total, halo)
-    _done(rewards)
-    return out
+    return kind, boot
