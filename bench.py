@@ -407,9 +407,12 @@ def config_dict(cfg, world, split, n_sets, per_set, use_graph):
 
 
 def run_reference(args, world, rank):
-    cfg = CONFIGS[args.config]
     if rank != 0:
         return
+    if args.config not in CONFIGS:
+        print(json.dumps({"impl": "reference", "unavailable": f"{args.config}: no CPU arm for this harness"}))
+        return
+    cfg = CONFIGS[args.config]
     from oracle import oracle as orc
 
     split = world > 1 and cfg.get("split", False)
@@ -938,6 +941,115 @@ def run_b200(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# PPO-step harness: the estimators' share of a whole PPO update.
+PPO = dict(N=4096, T=128, obs_dim=64, act_dim=4, hidden=256, epochs=4, minibatches=4, clip=0.2, lr=3e-4)
+
+
+def _ppo_net(dev):
+    torch.manual_seed(0)
+    net = torch.nn.ModuleDict({
+        "body": torch.nn.Sequential(torch.nn.Linear(PPO["obs_dim"], PPO["hidden"]), torch.nn.Tanh(),
+                                    torch.nn.Linear(PPO["hidden"], PPO["hidden"]), torch.nn.Tanh()),
+        "pi": torch.nn.Linear(PPO["hidden"], PPO["act_dim"]),
+        "v": torch.nn.Linear(PPO["hidden"], 1),
+    }).to(dev)
+    log_std = torch.zeros(PPO["act_dim"], device=dev, requires_grad=True)
+    return net, log_std
+
+
+def _ppo_rollout(dev, seed):
+    """bf16 rollout buffers of a continuous-action task (seeded synthetic data)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n, t = PPO["N"], PPO["T"]
+    return dict(obs=torch.randn(n, t, PPO["obs_dim"], generator=g, device=dev).to(torch.bfloat16),
+                act=torch.randn(n, t, PPO["act_dim"], generator=g, device=dev).to(torch.bfloat16),
+                old_logp=(-torch.rand(n, t, generator=g, device=dev) * 4).to(torch.bfloat16),
+                rew=torch.randn(n, t, generator=g, device=dev).to(torch.bfloat16),
+                done=(torch.rand(n, t, generator=g, device=dev) < 0.01).to(torch.bfloat16))
+
+
+def ppo_update(net, log_std, opt, ro, estimator, ev=None):
+    """One PPO update: values of the rollout, the estimator (GAE, advantage
+    normalisation, returns), then epochs x minibatches of clipped-surrogate +
+    value loss, backward and Adam.  `ev` = (start, end) events around the
+    estimator."""
+    import rl_triton
+
+    n, t = PPO["N"], PPO["T"]
+    flat_obs = ro["obs"].reshape(n * t, -1)
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        values = net["v"](net["body"](flat_obs)).reshape(n, t)
+    if ev:
+        ev[0].record()
+    if estimator == "fused":
+        adv, ret = rl_triton.compute_gae_normalized(ro["rew"], values, ro["done"], gamma=0.99, lambda_=0.95,
+                                                    return_returns=True)
+    else:
+        a = rl_triton.compute_gae(ro["rew"], values, ro["done"], gamma=0.99, lambda_=0.95)
+        ret = a + values.float()
+        adv = (a - a.mean()) / (a.std() + 1e-8)
+    if ev:
+        ev[1].record()
+    adv, ret = adv.reshape(-1), ret.reshape(-1)
+    act = ro["act"].reshape(n * t, -1).float()
+    old_logp = ro["old_logp"].reshape(-1).float()
+    mb = n * t // PPO["minibatches"]
+    for _ in range(PPO["epochs"]):
+        perm = torch.randperm(n * t, device=adv.device)
+        for k in range(PPO["minibatches"]):
+            idx = perm[k * mb:(k + 1) * mb]
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                h = net["body"](flat_obs[idx])
+                mean, v = net["pi"](h).float(), net["v"](h).float().squeeze(-1)
+            logp = (-0.5 * ((act[idx] - mean) / log_std.exp()) ** 2 - log_std).sum(-1)
+            ratio = (logp - old_logp[idx]).exp()
+            surr = torch.min(ratio * adv[idx], ratio.clamp(1 - PPO["clip"], 1 + PPO["clip"]) * adv[idx])
+            loss = -surr.mean() + 0.5 * ((v - ret[idx]) ** 2).mean()
+            opt.zero_grad(set_to_none=True)
+            loss.backward()
+            opt.step()
+
+
+def run_ppo(args, local):
+    """`--config ppo`: PPO updates on 4096 x 128 bf16 rollouts; the estimator
+    is the fused normalising GAE (`fused`) or GAE + PyTorch normalisation
+    (`unfused`).  Reports update throughput and the estimator's share."""
+    dev = torch.device("cuda", local)
+    ro = _ppo_rollout(dev, 0)
+    res = {}
+    for est in ("fused", "unfused"):
+        net, log_std = _ppo_net(dev)
+        opt = torch.optim.Adam(list(net.parameters()) + [log_std], lr=PPO["lr"])
+        for _ in range(args.warmup):
+            ppo_update(net, log_std, opt, ro, est)
+        torch.cuda.synchronize(dev)
+        tot, est_ms = [], []
+        for _ in range(args.steps):
+            e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            e[0].record()
+            ppo_update(net, log_std, opt, ro, est, ev=(e[1], e[2]))
+            e[3].record()
+            torch.cuda.synchronize(dev)
+            tot.append(e[0].elapsed_time(e[3]))
+            est_ms.append(e[1].elapsed_time(e[2]))
+        t_ms, e_ms = statistics.median(tot), statistics.median(est_ms)
+        res[est] = {"ms_per_update": round(t_ms, 4), "estimator_ms": round(e_ms, 4),
+                    "estimator_share": round(e_ms / t_ms, 4)}
+    n, t = PPO["N"], PPO["T"]
+    line = {"metric": "timesteps/sec", "value": n * t / (res["fused"]["ms_per_update"] / 1e3), "unit": "timesteps/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["fused"]["ms_per_update"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 rollout buffers, fp32 estimator arithmetic",
+            "data": "synthetic (seeded torch.Generator)",
+            "config": {"workload": "PPO update: 4096 x 128 bf16 rollout, MLP 64-256-256 policy/value, "
+                                   f"{PPO['epochs']} epochs x {PPO['minibatches']} minibatches, Adam",
+                       "timing": "CUDA events around each eager update (median) and around the estimator"},
+            "ppo": res,
+            "estimator_speedup_fused_vs_unfused": round(res["unfused"]["estimator_ms"] / res["fused"]["estimator_ms"], 3)}
+    print(json.dumps(line), flush=True)
+
+
 def run_ncu(args, local):
     cfg = CONFIGS[args.config]
     if args.envs:
@@ -997,7 +1109,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS) + ["ppo"])
     ap.add_argument("--sets", type=int, default=0, help="input sets to rotate (default: enough to exceed L2)")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -1032,6 +1144,9 @@ def main():
     try:
         if args.ncu:
             run_ncu(args, local)
+            return
+        if args.config == "ppo":
+            run_ppo(args, local)
             return
         run_b200(args, world, rank, local)
     finally:

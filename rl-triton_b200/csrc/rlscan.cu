@@ -362,8 +362,15 @@ struct Rows2L {
       constexpr int W = P::kOuts > 1 ? 4 : 8;
       return launch_rowk(rows1_kernel<P, W>, (g.N + W - 1) / W, W * 32, s, g, p.out0, p.out1, p, g);
     }
+    // Grids of many waves (e.g. 131072 x 1024) gain nothing from overlapping
+    // launches, and dependents parked in griddepcontrol.wait would hold SM
+    // slots during the tail: launch them plainly.
     const int64_t blocks = (g.N + 3) / 4;
-    return launch_rowk(rows2_kernel<P, 4, 1>, blocks, 128, s, g, p.out0, p.out1, p, g);
+    Geom g2 = g;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
+    if (blocks > 16LL * num_sms(dev)) g2.pdl = 0;
+    return launch_rowk(rows2_kernel<P, 4, 1>, blocks, 128, s, g2, p.out0, p.out1, p, g2);
   }
 };
 
