@@ -502,6 +502,33 @@ def time_function(calls, fname, stream, use_graph, min_reps=8, max_reps=1000, bu
     return out
 
 
+def time_fused(sets, stream, use_graph, world, hbm):
+    """GAE + batch advantage normalisation + returns, fused (one call) and
+    composed from compute_gae and PyTorch ops, on the rotating input sets."""
+    import rl_triton
+
+    def composed(x):
+        a = rl_triton.compute_gae(x["r"], x["v"], x["term"], gamma=0.99, lambda_=0.95)
+        ret = a + x["v"].float()
+        return (a - a.mean()) / (a.std() + 1e-8), ret
+
+    calls = [{"fused": (lambda x=x: rl_triton.compute_gae_normalized(x["r"], x["v"], x["term"], gamma=0.99,
+                                                                      lambda_=0.95, return_returns=True)),
+              "composed": (lambda x=x: composed(x))} for x in sets]
+    x0 = sets[0]
+    n, t = x0["r"].shape
+    esz = x0["r"].element_size()
+    alg = (3 * esz + 8) * n * t  # r, v, term in; normalised advantages and returns out
+    out = {"workload": "advantages normalised over the batch + returns (A + V)",
+           "algorithmic_bytes": alg}
+    for name in ("fused", "composed"):
+        r = time_function(calls, name, stream, use_graph, fixed_reps=8 if world > 1 else 0)
+        out[name] = {"us_per_call": r["us_per_launch"], "full_call_us": r["full_call_us"],
+                     "frac_of_peak": round(alg / (r["us_per_launch"] * 1e-6) / 1e9 / hbm, 4)}
+    out["speedup"] = round(out["composed"]["us_per_call"] / out["fused"]["us_per_call"], 3)
+    return out
+
+
 def sample_window(cfg):
     """Rows and columns of an output compared across the two GPU arms."""
     rows = min(cfg["N"], max(1, (1 << 22) // cfg["T"]))
@@ -884,6 +911,11 @@ def run_b200(args, world, rank, local):
     d = per_fn[dom]
     traffic = read_traffic(dom, args.config)
 
+    # The fused epilogues against the same work composed from separate calls.
+    fused = None
+    if not args.no_fused and not split and not cfg["trunc"] and "gae" in cfg["funcs"]:
+        fused = time_fused(sets, stream, use_graph, world, hbm)
+
     # Parity of the timed path's outputs.
     parity = None if args.no_parity else check_parity(cfg, sets[0], calls[0], split, world, rank)
 
@@ -929,6 +961,7 @@ def run_b200(args, world, rank, local):
                          else "fallback 6650 GB/s",
                          "context": rw},
             "per_function": per_fn,
+            "fused": fused,
             "parity": parity,
             "triton_reference": tri,
             "clocks": clocks,
@@ -1017,15 +1050,17 @@ def run_ppo(args, local):
     (`unfused`).  Reports update throughput and the estimator's share."""
     dev = torch.device("cuda", local)
     ro = _ppo_rollout(dev, 0)
-    res = {}
+    arms = {}
     for est in ("fused", "unfused"):
         net, log_std = _ppo_net(dev)
         opt = torch.optim.Adam(list(net.parameters()) + [log_std], lr=PPO["lr"])
         for _ in range(args.warmup):
             ppo_update(net, log_std, opt, ro, est)
-        torch.cuda.synchronize(dev)
-        tot, est_ms = [], []
-        for _ in range(args.steps):
+        arms[est] = (net, log_std, opt, [], [])
+    torch.cuda.synchronize(dev)
+    for k in range(args.steps):  # the arms alternate, in alternating order
+        for est in (("fused", "unfused") if k % 2 == 0 else ("unfused", "fused")):
+            net, log_std, opt, tot, est_ms = arms[est]
             e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
             e[0].record()
             ppo_update(net, log_std, opt, ro, est, ev=(e[1], e[2]))
@@ -1033,6 +1068,8 @@ def run_ppo(args, local):
             torch.cuda.synchronize(dev)
             tot.append(e[0].elapsed_time(e[3]))
             est_ms.append(e[1].elapsed_time(e[2]))
+    res = {}
+    for est, (_, _, _, tot, est_ms) in arms.items():
         t_ms, e_ms = statistics.median(tot), statistics.median(est_ms)
         res[est] = {"ms_per_update": round(t_ms, 4), "estimator_ms": round(e_ms, 4),
                     "estimator_share": round(e_ms / t_ms, 4)}
@@ -1122,6 +1159,7 @@ def main():
     ap.add_argument("--len", type=int, default=0, help="--ncu mode: override the sequence length T")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the timed outputs")
     ap.add_argument("--no-triton", action="store_true", help="skip timing the reference's Triton kernels")
+    ap.add_argument("--no-fused", action="store_true", help="skip the fused-epilogue comparison")
     ap.add_argument("--no-sharded", action="store_true",
                     help="skip the config 4 (env-sharded) and 5b (time-split) legs of the default run")
     ap.add_argument("--triton-worker", action="store_true", help=argparse.SUPPRESS)

@@ -366,11 +366,14 @@ struct Rows2L {
     // launches, and dependents parked in griddepcontrol.wait would hold SM
     // slots during the tail: launch them plainly.
     const int64_t blocks = (g.N + 3) / 4;
-    Geom g2 = g;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
-    if (blocks > 16LL * num_sms(dev)) g2.pdl = 0;
-    return launch_rowk(rows2_kernel<P, 4, 1>, blocks, 128, s, g2, p.out0, p.out1, p, g2);
+    if (blocks > 16LL * num_sms(dev)) {
+      Geom g2 = g;
+      g2.pdl = 0;
+      return launch_rowk(rows2_kernel<P, 4, 1, false>, blocks, 128, s, g2, p.out0, p.out1, p, g2);
+    }
+    return launch_rowk(rows2_kernel<P, 4, 1, true>, blocks, 128, s, g, p.out0, p.out1, p, g);
   }
 };
 

@@ -265,8 +265,11 @@ __device__ __forceinline__ float rows2_chunk(const typename P::Params& p, const 
   return cs.pass2(p, g, ch, carry);
 }
 
-template <class P, int WPB, int R, int MINB = 1>
-__global__ void __launch_bounds__(WPB * 32, MINB) rows2_kernel(const typename P::Params p, const Geom g) {
+// PDL: launched with programmatic stream serialization (Geom::pdl says when the
+// first loads may precede the wait).  A separate instantiation keeps the wait
+// out of the plain kernel's code, whose register allocation it would change.
+template <class P, int WPB, int R, bool PDL = false>
+__global__ void __launch_bounds__(WPB * 32) rows2_kernel(const typename P::Params p, const Geom g) {
   constexpr int VEC = Rows2Chunk<P, R>::VEC;
   constexpr int64_t CH = (int64_t)R * 32 * VEC;
   constexpr bool BWD = P::kBackward;
@@ -281,13 +284,17 @@ __global__ void __launch_bounds__(WPB * 32, MINB) rows2_kernel(const typename P:
   Rows2Chunk<P, R> a, b;
   typename P::Nbr edge_nbr{};
   float carry = 0.f;
-  pdl_trigger();
-  if (g.pdl == 1) pdl_wait();
+  if constexpr (PDL) {
+    pdl_trigger();
+    if (g.pdl == 1) pdl_wait();
+  }
   rows2_load<P, R>(p, rbase, S, cb_of(0), lane, a);
+  if constexpr (PDL) {
+    if (g.pdl == 2) pdl_wait();  // the first chunk's loads are in flight; nothing is stored before this
+  }
   for (int64_t k = 0; k < nch; k += 2) {
     if (k + 1 < nch) rows2_load<P, R>(p, rbase, S, cb_of(k + 1), lane, b);
-    // pdl == 2: the first chunk is loaded and scanned before the wait; no store precedes it
-    carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k), lane, a, carry, edge_nbr, g.pdl == 2 && k == 0);
+    carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k), lane, a, carry, edge_nbr);
     if (k + 1 >= nch) break;
     if (k + 2 < nch) rows2_load<P, R>(p, rbase, S, cb_of(k + 2), lane, a);
     carry = rows2_chunk<P, R>(p, g, row, rbase, cb_of(k + 1), lane, b, carry, edge_nbr);
