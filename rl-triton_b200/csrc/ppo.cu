@@ -212,12 +212,30 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_norm_kernel(const typenam
 }
 
 // ---- large batches: statistics, then normalise ---------------------------------
+// Grid-stride over float4 groups, UNR groups per thread in flight per step so
+// the whole GPU keeps enough bytes in flight; M % 4 == 0 for the vector part,
+// the tail (< 4 elements) is handled by the first threads.
+constexpr int kStatUnroll = 4;
 __global__ void __launch_bounds__(kStatThreads) norm_stats_kernel(const float* adv, int64_t M, double2* partials) {
   double a = 0.0, b = 0.0;
-  const int64_t per = (M + gridDim.x - 1) / gridDim.x;
-  const int64_t lo = (int64_t)blockIdx.x * per, hi = lo + per < M ? lo + per : M;
-  for (int64_t i = lo + threadIdx.x; i < hi; i += kStatThreads) {
-    const float v = __ldcg(adv + i);
+  const int64_t M4 = M / 4;
+  const float4* a4 = reinterpret_cast<const float4*>(adv);
+  const int64_t stride = (int64_t)gridDim.x * kStatThreads;
+  for (int64_t g0 = (int64_t)blockIdx.x * kStatThreads + threadIdx.x; g0 < M4; g0 += stride * kStatUnroll) {
+    float4 v[kStatUnroll];
+#pragma unroll
+    for (int u = 0; u < kStatUnroll; ++u) {
+      const int64_t gi = g0 + u * stride;
+      v[u] = gi < M4 ? __ldcg(a4 + gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kStatUnroll; ++u) {
+      a += (double)v[u].x + (double)v[u].y + (double)v[u].z + (double)v[u].w;
+      b += (double)v[u].x * v[u].x + (double)v[u].y * v[u].y + (double)v[u].z * v[u].z + (double)v[u].w * v[u].w;
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (unsigned)(M - M4 * 4)) {
+    const float v = adv[M4 * 4 + threadIdx.x];
     a += v;
     b += (double)v * v;
   }
@@ -242,8 +260,33 @@ __global__ void __launch_bounds__(kStatThreads) norm_apply_kernel(const float* a
   }
   __syncthreads();
   const float mean = s_mean, den = s_den;
-  for (int64_t i = (int64_t)blockIdx.x * kStatThreads + threadIdx.x; i < M; i += (int64_t)gridDim.x * kStatThreads) {
-    const float a = __ldcs(adv + i);
+  const int64_t M4 = M / 4;
+  const float4* a4 = reinterpret_cast<const float4*>(adv);
+  const int64_t stride = (int64_t)gridDim.x * kStatThreads;
+  for (int64_t g0 = (int64_t)blockIdx.x * kStatThreads + threadIdx.x; g0 < M4; g0 += stride * kStatUnroll) {
+    float4 v[kStatUnroll];
+#pragma unroll
+    for (int u = 0; u < kStatUnroll; ++u) {
+      const int64_t gi = g0 + u * stride;
+      v[u] = gi < M4 ? __ldcs(a4 + gi) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kStatUnroll; ++u) {
+      const int64_t gi = g0 + u * stride;
+      if (gi >= M4) break;
+      const int64_t i = gi * 4;
+      if (na.rets)
+        st_stream_f4(na.rets + i, make_float4(v[u].x + load_value(na.values, na.bf16, i),
+                                              v[u].y + load_value(na.values, na.bf16, i + 1),
+                                              v[u].z + load_value(na.values, na.bf16, i + 2),
+                                              v[u].w + load_value(na.values, na.bf16, i + 3)));
+      st_stream_f4(na.norm + i, make_float4((v[u].x - mean) / den, (v[u].y - mean) / den, (v[u].z - mean) / den,
+                                            (v[u].w - mean) / den));
+    }
+  }
+  if (blockIdx.x == 0 && threadIdx.x < (unsigned)(M - M4 * 4)) {
+    const int64_t i = M4 * 4 + threadIdx.x;
+    const float a = adv[i];
     if (na.rets) na.rets[i] = a + load_value(na.values, na.bf16, i);
     na.norm[i] = (a - mean) / den;
   }
@@ -470,7 +513,9 @@ extern "C" int rls_gae_normalized(const void* rewards, const void* values, const
   // Too large for one on-chip pass: GAE into the advantages (or the output as
   // scratch), then statistics and normalisation.
   float* adv = advantages ? advantages : normalized;
-  const int nparts = 4 * num_sms_of(0);
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return RLS_ECUDA;
+  const int nparts = 8 * num_sms_of(cur);
   if ((size_t)64 + (size_t)nparts * sizeof(double2) > ws_bytes) return RLS_EWORKSPACE;
   st = rls_gae(rewards, values, terminateds, truncateds, bootstrap, boot_kind, adv, num_envs, seq_len, gamma,
                lambda_, in_dtype, nullptr, ws, ws_bytes, stream);
@@ -580,7 +625,9 @@ extern "C" int rls_gae_value_loss(const void* rewards, const void* values, const
   if (st) return st;
   st = prepare_layout(ws, ws_bytes, kLayoutScratch, s);
   if (st) return st;
-  const int nparts = 4 * num_sms_of(0);
+  int cur = 0;
+  if (cudaGetDevice(&cur) != cudaSuccess) return RLS_ECUDA;
+  const int nparts = 8 * num_sms_of(cur);
   if ((size_t)64 + (size_t)nparts * sizeof(double) > ws_bytes) return RLS_EWORKSPACE;
   value_loss_elementwise<<<nparts, kStatThreads, 0, s>>>(adv, g.M, va);
   value_loss_finish<<<1, kStatThreads, 0, s>>>(va.partials, nparts, va.inv_count, loss);
