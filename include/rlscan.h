@@ -184,12 +184,11 @@ int rls_affine_scan(const float* u, const float* v, const float* carry, int dire
  *   mean = sum(A) / M,  std = sqrt(sum((A - mean)^2) / (M - 1))  (M = N*T,
  *   unbiased like torch.std),  normalized = (A - mean) / (std + eps).
  * Optional outputs (NULL to skip): returns = A + V (the value targets), the
- * raw advantages A, and stats = fp32[2] {mean, std}.  When the batch fits in
- * shared memory across one wave of CTAs (e.g. 4096 x 128, 4096 x 1024) one
- * cooperative kernel reads the inputs once and writes the outputs once;
- * larger batches take GAE, a statistics pass and a normalise pass.  The
- * workspace (as for rls_gae) also holds the fp64 partial sums and a grid
- * barrier counter.  Results are deterministic.                               */
+ * raw advantages A, and stats = fp32[2] {mean, std}.  Two launches: GAE with
+ * per-CTA fp64 partial sums (the advantages go to `advantages`, or to
+ * `normalized` as scratch), then the normalisation; rows that do not start
+ * 16-byte aligned take one more pass.  The workspace (as for rls_gae) holds
+ * the partial sums.  Results are deterministic.                               */
 int rls_gae_normalized(const void* rewards, const void* values, const void* terminateds,
                        const void* truncateds, const void* bootstrap, int boot_kind,
                        float* normalized, float* returns, float* advantages, float* stats,

@@ -7,14 +7,13 @@
 //   norm = (A - mean) / (std + eps)   (torch: (A - A.mean()) / (A.std() + eps)),
 // plus, optionally, the value targets A + V and the raw advantages.
 //
-// Single pass when the batch fits on chip: a cooperative, persistent grid of
-// 8-warp CTAs (one wave) scans the rows (one warp per row, the lean row
-// kernel's chunk walk), keeps the advantages in shared memory, reduces
-// (sum, sum of squares) per CTA in fp64, meets at one grid barrier, reduces the
-// CTA partials in a fixed order (every CTA gets the same mean and std), then
-// normalises its rows from shared memory and writes them once: the same HBM
-// bytes as GAE alone.  Larger batches: GAE, then a statistics kernel and a
-// normalise kernel (the advantages are read twice more).  Both paths are
+// Two passes, both launched with programmatic dependent launch so they overlap
+// their neighbours' launch and tail: pass 1 is GAE (the row kernels' chunk
+// walk) writing the advantages with ordinary stores -- at RL batch sizes they
+// stay in the 126 MB L2 -- and one fp64 (sum, sum of squares) per CTA; pass 2
+// reduces the CTA partials in a fixed order (every CTA gets the same mean and
+// std) and writes the normalised advantages and the returns.  Rows that do not
+// start 16-byte aligned take GAE, a statistics pass and a normalise pass.  All
 // deterministic (no floating-point atomics).
 #include <cmath>
 #include <cstdint>
@@ -41,10 +40,6 @@ struct NormArgs {
   const void* values;   // V, for the returns
   int bf16;
   double2* partials;    // per CTA (sum, sum of squares)
-  unsigned* bar_count;  // grid barrier: arrivals of the current generation
-  unsigned* bar_gen;    // grid barrier: generation
-  unsigned* error;      // bounded-wait error latch (bit 4: grid barrier)
-  int rows_per_warp;
   float eps;
 };
 
@@ -79,38 +74,6 @@ __device__ __forceinline__ void walk_row(const typename P::Params& p, const Geom
     const int64_t col0 = cs.col0[0];
     carry = cs.pass2(p, g, ch[k & 1], carry, [&](int, int q, float4 v0, float4) { sink(col0 + q, v0); });
   }
-}
-
-// Grid barrier for a cooperative launch (all CTAs resident).  Bounded: a wait
-// that runs out latches error bit 4 and returns false (results then invalid).
-__device__ bool grid_barrier(const NormArgs& na) {
-  __shared__ int s_ok;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned gen0 = ld_acquire_u32(na.bar_gen);
-    __threadfence();
-    const unsigned arrived = atomicAdd(na.bar_count, 1u);
-    int ok = 1;
-    if (arrived == gridDim.x - 1) {
-      *na.bar_count = 0u;
-      __threadfence();
-      atomicAdd(na.bar_gen, 1u);
-    } else {
-      unsigned spins = 0;
-      while (ld_acquire_u32(na.bar_gen) == gen0) {
-        if (++spins > kSpinLimit) {
-          ok = 0;
-          atomicOr(na.error, 4u);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    __threadfence();
-    s_ok = ok;
-  }
-  __syncthreads();
-  return s_ok != 0;
 }
 
 // Block-wide fp64 sum of (a, b); every thread gets the result.  Fixed order.
@@ -152,37 +115,52 @@ __device__ void finish_stats(const double2* partials, int n, int64_t count, floa
   *den_f = *std_f + eps;
 }
 
+// Pass 1 (one warp per row, rows strided over the grid): GAE into `tmp` with
+// ordinary stores (at RL batch sizes the advantages stay in L2 for pass 2) and
+// the per-CTA fp64 (sum, sum of squares).  Launched with programmatic stream
+// serialization: it triggers its dependents at once and waits for its
+// predecessor before its first store (and before its first load when an input
+// may be the predecessor's output, Geom::pdl == 1).
 template <class P>
-__global__ void __launch_bounds__(kNormWarps * 32) gae_norm_kernel(const typename P::Params p, const Geom g,
-                                                                    const NormArgs na) {
-  extern __shared__ float4 sm4[];
+__global__ void __launch_bounds__(kNormWarps * 32) gae_stats_kernel(const typename P::Params p, const Geom g,
+                                                                     float* tmp, double2* partials) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t S = g.S;
-  float* mine = reinterpret_cast<float*>(sm4) + (size_t)warp * na.rows_per_warp * S;
   const int64_t W = (int64_t)gridDim.x * kNormWarps;
-  const int64_t gw = (int64_t)blockIdx.x * kNormWarps + warp;
+  pdl_trigger();
+  if (g.pdl == 1) pdl_wait();
+  bool waited = g.pdl == 1;
   double s1 = 0.0, s2 = 0.0;
-  for (int j = 0; j < na.rows_per_warp; ++j) {
-    const int64_t row = gw + (int64_t)j * W;
-    if (row >= g.N) break;
-    float* rs = mine + (size_t)j * S;
+  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < g.N; row += W) {
     walk_row<P>(p, g, row, lane, [&](int64_t col, float4 v) {
-      *reinterpret_cast<float4*>(rs + col) = v;
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
+      *reinterpret_cast<float4*>(tmp + row * S + col) = v;
       s1 += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
       s2 += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
     });
   }
   const double2 part = block_sum2<kNormWarps * 32>(s1, s2);
-  if (threadIdx.x == 0) na.partials[blockIdx.x] = part;
-  grid_barrier(na);
-  __shared__ float s_mean, s_den, s_std;
+  pdl_wait();  // also in CTAs that stored nothing: the partials follow the predecessor
+  if (threadIdx.x == 0) partials[blockIdx.x] = part;
+}
+
+// Pass 2: every CTA reduces the partials in the same fixed order (identical
+// mean and std everywhere), then normalises its float4 groups of `tmp` (which
+// may be `norm` itself) and writes the returns.  Waits for pass 1 first.
+__global__ void __launch_bounds__(kStatThreads) norm_finish_kernel(const float* tmp, int64_t M,
+                                                                   const double2* partials, int nparts, NormArgs na) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float s_mean, s_den;
   {
     float m, d, sd;
-    finish_stats<kNormWarps * 32>(na.partials, gridDim.x, g.M, na.eps, &m, &d, &sd);
+    finish_stats<kStatThreads>(partials, nparts, M, na.eps, &m, &d, &sd);
     if (threadIdx.x == 0) {
       s_mean = m;
       s_den = d;
-      s_std = sd;
       if (blockIdx.x == 0 && na.stats) {
         na.stats[0] = m;
         na.stats[1] = sd;
@@ -191,23 +169,24 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_norm_kernel(const typenam
   }
   __syncthreads();
   const float mean = s_mean, den = s_den;
-  __syncwarp();
-  for (int j = 0; j < na.rows_per_warp; ++j) {
-    const int64_t row = gw + (int64_t)j * W;
-    if (row >= g.N) break;
-    const float* rs = mine + (size_t)j * S;
-    for (int64_t c = (int64_t)lane * 4; c < S; c += 128) {
-      const float4 a = *reinterpret_cast<const float4*>(rs + c);
-      const int64_t i = row * S + c;
-      st_stream_f4(na.norm + i, make_float4((a.x - mean) / den, (a.y - mean) / den, (a.z - mean) / den,
-                                            (a.w - mean) / den));
-      if (na.raw) st_stream_f4(na.raw + i, a);
-      if (na.rets)
-        st_stream_f4(na.rets + i, make_float4(a.x + load_value(na.values, na.bf16, i),
-                                              a.y + load_value(na.values, na.bf16, i + 1),
-                                              a.z + load_value(na.values, na.bf16, i + 2),
-                                              a.w + load_value(na.values, na.bf16, i + 3)));
+  const int64_t M4 = M / 4;  // rows are a multiple of 4 steps on this path
+  const int64_t stride = (int64_t)gridDim.x * kStatThreads;
+  for (int64_t gi = (int64_t)blockIdx.x * kStatThreads + threadIdx.x; gi < M4; gi += stride) {
+    const int64_t i = gi * 4;
+    const float4 a = __ldcs(reinterpret_cast<const float4*>(tmp + i));
+    if (na.rets) {
+      float4 v;
+      if (na.bf16) {
+        const uint2 u = __ldcs(reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned short*>(na.values) + i));
+        v = make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
+                        __uint_as_float(u.y & 0xffff0000u));
+      } else {
+        v = __ldcs(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(na.values) + i));
+      }
+      st_stream_f4(na.rets + i, make_float4(a.x + v.x, a.y + v.y, a.z + v.z, a.w + v.w));
     }
+    st_stream_f4(na.norm + i, make_float4((a.x - mean) / den, (a.y - mean) / den, (a.z - mean) / den,
+                                          (a.w - mean) / den));
   }
 }
 
@@ -391,48 +370,30 @@ int num_sms_of(int dev) {
   return cache[dev];
 }
 
-constexpr size_t kNormSmemMax = 200 * 1024;
-
-// Cooperative single pass; returns RLS_EUNSUPPORTED when the batch does not fit
-// on chip in one wave.
+// The two passes; RLS_EUNSUPPORTED for rows that do not start 16-byte aligned.
 template <class P>
-int launch_gae_norm(const typename P::Params& p, const Geom& g, NormArgs na, size_t ws_bytes, cudaStream_t s) {
+int launch_gae_norm(const typename P::Params& p, Geom g, NormArgs na, size_t ws_bytes, cudaStream_t s) {
   constexpr int VEC = Rows2Chunk<P, 1>::VEC;
   if (g.S % VEC != 0) return RLS_EUNSUPPORTED;
-  auto kern = gae_norm_kernel<P>;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
-  static bool attr_set[64] = {false};
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNormSmemMax) != cudaSuccess)
-      return RLS_ECUDA;
-    attr_set[dev] = true;
-  }
   const int sms = num_sms_of(dev);
-  for (int rpw = 1;; ++rpw) {
-    const size_t smem = (size_t)kNormWarps * rpw * g.S * sizeof(float);
-    if (smem > kNormSmemMax) return RLS_EUNSUPPORTED;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kNormWarps * 32, smem) != cudaSuccess)
-      return RLS_ECUDA;
-    if (per_sm < 1) return RLS_EUNSUPPORTED;
-    const int64_t warps_needed = (g.N + rpw - 1) / rpw;
-    const int64_t blocks = (warps_needed + kNormWarps - 1) / kNormWarps;
-    if (blocks > (int64_t)per_sm * sms) continue;
-    if ((size_t)64 + (size_t)blocks * sizeof(double2) > ws_bytes) return RLS_EWORKSPACE;
-    na.rows_per_warp = rpw;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)blocks);
-    cfg.blockDim = dim3(kNormWarps * 32);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, p, g, na) == cudaSuccess ? RLS_OK : RLS_ECUDA;
-  }
+  int64_t blocks = (g.N + kNormWarps - 1) / kNormWarps;
+  if (blocks > 8LL * sms) blocks = 8LL * sms;
+  if ((size_t)64 + (size_t)blocks * sizeof(double2) > ws_bytes) return RLS_EWORKSPACE;
+  float* tmp = na.raw ? na.raw : na.norm;
+  const size_t mb = (size_t)g.M * (na.bf16 ? 2 : 4);
+  g.pdl = pdl_mode(s, {{p.r, mb}, {p.v, mb}, {p.term, mb}, {p.trunc, mb}, {p.boot, mb},
+                       {p.boot_row, (size_t)g.N * 4}});
+  int st = launch_rowk(gae_stats_kernel<P>, blocks, kNormWarps * 32, s, g.pdl, g.M, tmp, nullptr, p, g, tmp,
+                       na.partials);
+  if (st) return st;
+  const int64_t groups = g.M / 4;
+  int64_t fb = (groups + kStatThreads * 4 - 1) / (kStatThreads * 4);
+  if (fb > 2LL * sms) fb = 2LL * sms;
+  if (fb < 1) fb = 1;
+  return launch_rowk(norm_finish_kernel, fb, kStatThreads, s, 1, g.M, na.norm, na.rets, (const float*)tmp, g.M,
+                     (const double2*)na.partials, (int)blocks, na);
 }
 
 template <class T>
@@ -476,7 +437,6 @@ extern "C" int rls_gae_normalized(const void* rewards, const void* values, const
   g.S = seq_len;
   g.N = num_envs;
   g.edge_global = 1;
-  WsHeader* hdr = reinterpret_cast<WsHeader*>(ws);
   NormArgs na{};
   na.norm = normalized;
   na.rets = returns;
@@ -485,9 +445,6 @@ extern "C" int rls_gae_normalized(const void* rewards, const void* values, const
   na.values = values;
   na.bf16 = in_dtype == RLS_BF16;
   na.partials = reinterpret_cast<double2*>(static_cast<char*>(ws) + 64);
-  na.bar_count = &hdr->pad[0];
-  na.bar_gen = &hdr->pad[1];
-  na.error = &hdr->error;
   na.eps = eps;
 
 #define NORM_PARAMS(T)                                                                                    \
@@ -510,8 +467,8 @@ extern "C" int rls_gae_normalized(const void* rewards, const void* values, const
 #undef NORM_PARAMS
   if (st != RLS_EUNSUPPORTED) return st;
 
-  // Too large for one on-chip pass: GAE into the advantages (or the output as
-  // scratch), then statistics and normalisation.
+  // Rows that do not start 16-byte aligned: GAE into the advantages (or the
+  // output as scratch), then a statistics pass and a normalise pass.
   float* adv = advantages ? advantages : normalized;
   int cur = 0;
   if (cudaGetDevice(&cur) != cudaSuccess) return RLS_ECUDA;

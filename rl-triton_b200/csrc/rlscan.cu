@@ -56,6 +56,61 @@ int prepare_layout(void* ws, size_t wsb, int layout, cudaStream_t s) {
   }
   return RLS_OK;
 }
+
+// ---- programmatic dependent launch of the row kernels ------------------------
+// The row kernels (one warp per row, no workspace) are launched with
+// programmatic stream serialization: the next one's launch and CTA ramp overlap
+// the tail of the one before, which at 4096 x 128 is most of a launch.  A
+// kernel waits (griddepcontrol.wait) for the preceding grid before its first
+// store, and before its first load unless none of its inputs can be an output
+// of the preceding library launch on the stream.  Only the row kernels trigger
+// their dependents early; any other preceding kernel (this library's or not)
+// completes before a dependent starts, so the overlap check needs only the
+// outputs of the last row-kernel launch per stream, kept here under the launch
+// lock.
+struct PdlRange {
+  uintptr_t lo, hi;
+};
+struct PdlRecord {
+  cudaStream_t s;
+  PdlRange out[2];
+  bool used;
+};
+static PdlRecord g_pdl[64];
+static int g_pdl_next = 0;
+
+static PdlRecord* pdl_find(cudaStream_t s) {
+  for (auto& r : g_pdl)
+    if (r.used && r.s == s) return &r;
+  return nullptr;
+}
+
+// 2: the inputs are disjoint from the last row-kernel outputs on this stream
+// (loads may start before the wait); 1: they may overlap (wait first).
+int pdl_mode(cudaStream_t s, std::initializer_list<PdlIn> ins) {
+  const PdlRecord* r = pdl_find(s);
+  if (!r) return 2;
+  for (const PdlIn& in : ins) {
+    if (!in.p || !in.bytes) continue;
+    const uintptr_t lo = (uintptr_t)in.p, hi = lo + in.bytes;
+    for (const PdlRange& o : r->out)
+      if (o.lo < hi && lo < o.hi) return 1;
+  }
+  return 2;
+}
+
+void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes) {
+  PdlRecord* r = pdl_find(s);
+  if (!r) {
+    r = &g_pdl[g_pdl_next];
+    g_pdl_next = (g_pdl_next + 1) % 64;
+    r->s = s;
+    r->used = true;
+  }
+  r->out[0] = PdlRange{(uintptr_t)out0, out0 ? (uintptr_t)out0 + bytes : 0};
+  r->out[1] = PdlRange{(uintptr_t)out1, out1 ? (uintptr_t)out1 + bytes : 0};
+}
+
 }  // namespace rls
 
 namespace {
@@ -106,89 +161,6 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
 }
 
-// ---- programmatic dependent launch of the row kernels ------------------------
-// The row kernels (one warp per row, no workspace) are launched with
-// programmatic stream serialization: the next one's launch and CTA ramp overlap
-// the tail of the one before, which at 4096 x 128 is most of a launch.  A
-// kernel waits (griddepcontrol.wait) for the preceding grid before its first
-// store, and before its first load unless none of its inputs can be an output
-// of the preceding library launch on the stream.  Only the row kernels trigger
-// their dependents early; any other preceding kernel (this library's or not)
-// completes before a dependent starts, so the overlap check needs only the
-// outputs of the last row-kernel launch per stream, kept here under the launch
-// lock.
-struct PdlRange {
-  uintptr_t lo, hi;
-};
-struct PdlRecord {
-  cudaStream_t s;
-  PdlRange out[2];
-  bool used;
-};
-PdlRecord g_pdl[64];
-int g_pdl_next = 0;
-
-PdlRecord* pdl_find(cudaStream_t s) {
-  for (auto& r : g_pdl)
-    if (r.used && r.s == s) return &r;
-  return nullptr;
-}
-
-struct PdlIn {
-  const void* p;
-  size_t bytes;
-};
-// 2: the inputs are disjoint from the last row-kernel outputs on this stream
-// (loads may start before the wait); 1: they may overlap (wait first).
-int pdl_mode(cudaStream_t s, std::initializer_list<PdlIn> ins) {
-  const PdlRecord* r = pdl_find(s);
-  if (!r) return 2;
-  for (const PdlIn& in : ins) {
-    if (!in.p || !in.bytes) continue;
-    const uintptr_t lo = (uintptr_t)in.p, hi = lo + in.bytes;
-    for (const PdlRange& o : r->out)
-      if (o.lo < hi && lo < o.hi) return 1;
-  }
-  return 2;
-}
-
-void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes) {
-  PdlRecord* r = pdl_find(s);
-  if (!r) {
-    r = &g_pdl[g_pdl_next];
-    g_pdl_next = (g_pdl_next + 1) % 64;
-    r->s = s;
-    r->used = true;
-  }
-  r->out[0] = PdlRange{(uintptr_t)out0, out0 ? (uintptr_t)out0 + bytes : 0};
-  r->out[1] = PdlRange{(uintptr_t)out1, out1 ? (uintptr_t)out1 + bytes : 0};
-}
-
-// Launch a row kernel: plain when g.pdl == 0, else with the PDL attribute.
-template <class... KArgs, class... Args>
-int launch_rowk(void (*kern)(KArgs...), int64_t blocks, int threads, cudaStream_t s, const Geom& g,
-                const float* out0, const float* out1, Args&&... args) {
-  if (blocks > 0x7fffffffLL) return RLS_EINVAL;
-  if (g.pdl == 0) {
-    kern<<<(unsigned)blocks, threads, 0, s>>>(std::forward<Args>(args)...);
-    if (cudaPeekAtLastError() != cudaSuccess) return RLS_ECUDA;
-  } else {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)blocks);
-    cfg.blockDim = dim3(threads);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) != cudaSuccess) return RLS_ECUDA;
-  }
-  pdl_record(s, out0, out1, (size_t)g.M * sizeof(float));
-  return RLS_OK;
-}
-
 // ---- row-parallel path ------------------------------------------------
 constexpr int kRowWarps = 4;  // rows (warps) per CTA of the row kernel
 
@@ -203,7 +175,7 @@ bool use_rows(const Geom& g) {
 template <class Alg, int R>
 int launch_rows_r(const typename Alg::Params& p, const Geom& g, cudaStream_t s) {
   const int64_t blocks = (g.N + kRowWarps - 1) / kRowWarps;
-  return launch_rowk(rows_kernel<Alg, kRowWarps, R>, blocks, kRowWarps * 32, s, g, p.out0, p.out1, p, g);
+  return launch_rowk(rows_kernel<Alg, kRowWarps, R>, blocks, kRowWarps * 32, s, g.pdl, g.M, p.out0, p.out1, p, g);
 }
 
 // Rounds per chunk: enough 16-byte vectors in flight per lane without
@@ -360,7 +332,7 @@ struct Rows2L {
     constexpr int64_t kChunk = 32 * (16 / (int)sizeof(typename P::InT));
     if (g.S <= kChunk) {
       constexpr int W = P::kOuts > 1 ? 4 : 8;
-      return launch_rowk(rows1_kernel<P, W>, (g.N + W - 1) / W, W * 32, s, g, p.out0, p.out1, p, g);
+      return launch_rowk(rows1_kernel<P, W>, (g.N + W - 1) / W, W * 32, s, g.pdl, g.M, p.out0, p.out1, p, g);
     }
     // Grids of many waves (e.g. 131072 x 1024) gain nothing from overlapping
     // launches, and dependents parked in griddepcontrol.wait would hold SM
@@ -371,9 +343,9 @@ struct Rows2L {
     if (blocks > 16LL * num_sms(dev)) {
       Geom g2 = g;
       g2.pdl = 0;
-      return launch_rowk(rows2_kernel<P, 4, 1, false>, blocks, 128, s, g2, p.out0, p.out1, p, g2);
+      return launch_rowk(rows2_kernel<P, 4, 1, false>, blocks, 128, s, 0, g2.M, p.out0, p.out1, p, g2);
     }
-    return launch_rowk(rows2_kernel<P, 4, 1, true>, blocks, 128, s, g, p.out0, p.out1, p, g);
+    return launch_rowk(rows2_kernel<P, 4, 1, true>, blocks, 128, s, g.pdl, g.M, p.out0, p.out1, p, g);
   }
 };
 
