@@ -152,8 +152,10 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_stats_kernel(const typena
 // may be `norm` itself) and writes the returns.  Waits for pass 1 first.
 __global__ void __launch_bounds__(kStatThreads) norm_finish_kernel(const float* tmp, int64_t M,
                                                                    const double2* partials, int nparts, NormArgs na) {
-  pdl_trigger();
+  // Trigger only after the wait: a dependent then starts after pass 1 has
+  // completed, so it may read the raw advantages pass 1 wrote.
   pdl_wait();
+  pdl_trigger();
   __shared__ float s_mean, s_den;
   {
     float m, d, sd;
@@ -294,9 +296,16 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_value_kernel(const typena
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t S = g.S;
   const int64_t W = (int64_t)gridDim.x * kNormWarps;
+  pdl_trigger();
+  if (g.pdl == 1) pdl_wait();
+  bool waited = g.pdl == 1;
   double acc = 0.0;
   for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < g.N; row += W) {
     walk_row<P>(p, g, row, lane, [&](int64_t col, float4 a) {
+      if (!waited) {
+        pdl_wait();
+        waited = true;
+      }
       const int64_t i = row * S + col;
       const float av[4] = {a.x, a.y, a.z, a.w};
       const float4 nv4 = __ldcs(reinterpret_cast<const float4*>(va.new_v + i));
@@ -324,6 +333,7 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_value_kernel(const typena
     });
   }
   const double2 t = block_sum2<kNormWarps * 32>(acc, 0.0);
+  pdl_wait();  // also in CTAs that stored nothing
   if (threadIdx.x == 0) va.partials[blockIdx.x] = t.x;
 }
 
@@ -353,6 +363,8 @@ __global__ void __launch_bounds__(kStatThreads) value_loss_elementwise(const flo
 
 __global__ void __launch_bounds__(kStatThreads) value_loss_finish(const double* partials, int n, float inv_count,
                                                                   float* loss) {
+  pdl_wait();  // then trigger: a dependent starts after the loss pass has completed
+  pdl_trigger();
   double a = 0.0;
   for (int i = threadIdx.x; i < n; i += kStatThreads) a += __ldcg(partials + i);
   const double2 t = block_sum2<kStatThreads>(a, 0.0);
@@ -497,9 +509,14 @@ int launch_gae_value(const typename P::Params& p, const Geom& g, ValueArgs va, f
   const int64_t cap = (int64_t)8 * num_sms_of(dev);
   if (blocks > cap) blocks = cap;
   if ((size_t)64 + (size_t)blocks * sizeof(double) > ws_bytes) return RLS_EWORKSPACE;
-  gae_value_kernel<P><<<(unsigned)blocks, kNormWarps * 32, 0, s>>>(p, g, va);
-  value_loss_finish<<<1, kStatThreads, 0, s>>>(va.partials, (int)blocks, va.inv_count, loss);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  const size_t mb = (size_t)g.M * (va.bf16 ? 2 : 4);
+  Geom g2 = g;
+  g2.pdl = pdl_mode(s, {{p.r, mb}, {p.v, mb}, {p.term, mb}, {p.trunc, mb}, {p.boot, mb},
+                        {p.boot_row, (size_t)g.N * 4}, {va.new_v, (size_t)g.M * 4}});
+  int st = launch_rowk(gae_value_kernel<P>, blocks, kNormWarps * 32, s, g2.pdl, g.M, va.grad, va.rets, p, g2, va);
+  if (st) return st;
+  return launch_rowk(value_loss_finish, 1, kStatThreads, s, 1, 1, loss, nullptr, (const double*)va.partials,
+                     (int)blocks, va.inv_count, loss);
 }
 
 template <class T>
@@ -587,8 +604,11 @@ extern "C" int rls_gae_value_loss(const void* rewards, const void* values, const
   const int nparts = 8 * num_sms_of(cur);
   if ((size_t)64 + (size_t)nparts * sizeof(double) > ws_bytes) return RLS_EWORKSPACE;
   value_loss_elementwise<<<nparts, kStatThreads, 0, s>>>(adv, g.M, va);
-  value_loss_finish<<<1, kStatThreads, 0, s>>>(va.partials, nparts, va.inv_count, loss);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  if (cudaPeekAtLastError() != cudaSuccess) return RLS_ECUDA;
+  // value_loss_finish triggers its dependents: launched through launch_rowk so
+  // the stream's record names its output.
+  return launch_rowk(value_loss_finish, 1, kStatThreads, s, 1, 1, loss, nullptr, (const double*)va.partials, nparts,
+                     va.inv_count, loss);
 }
 
 // ---- GAE with observation-skip masking ---------------------------------------------
@@ -650,7 +670,7 @@ __device__ __forceinline__ void warp_suffix_scan(Pair m, int lane, Pair& excl, P
 template <class InT>
 __global__ void __launch_bounds__(kSkipWarps * 32) gae_obs_skip_kernel(const InT* r, const InT* v, const InT* mask,
                                                                         float* adv, float* rets, int64_t N, int64_t S,
-                                                                        float gamma, float gl) {
+                                                                        float gamma, float gl, int pdl) {
   constexpr int VEC = 16 / sizeof(InT);
   constexpr int64_t CH = 32 * VEC;
   const int lane = threadIdx.x & 31;
@@ -659,6 +679,9 @@ __global__ void __launch_bounds__(kSkipWarps * 32) gae_obs_skip_kernel(const InT
   const bool vec_ok = (S % VEC) == 0;
   const int64_t rbase = row * S;
   const int64_t nch = (S + CH - 1) / CH;
+  pdl_trigger();
+  if (pdl == 1) pdl_wait();
+  bool waited = pdl == 1;
   float carry_nv = 0.f, carry_a = 0.f;
   float next_m = 0.f, next_v = 0.f;  // m, V of the element after the current chunk
   for (int64_t k = 0; k < nch; ++k) {
@@ -721,6 +744,10 @@ __global__ void __launch_bounds__(kSkipWarps * 32) gae_obs_skip_kernel(const InT
     carry_a = apply(tot, carry_a);
     next_m = chunk_m0;
     next_v = chunk_v0;
+    if (!waited) {  // the first chunk is loaded and scanned; nothing is stored before the predecessor ends
+      pdl_wait();
+      waited = true;
+    }
     const int64_t i = rbase + col0;
     if (vec_ok && left >= VEC) {
 #pragma unroll
@@ -758,13 +785,14 @@ extern "C" int rls_gae_obs_skip(const void* rewards, const void* values, const v
   const int64_t blocks = (num_envs + kSkipWarps - 1) / kSkipWarps;
   if (blocks > 0x7fffffffLL) return RLS_EINVAL;
   const float gl = gamma * lambda_;
+  const size_t mb = (size_t)num_envs * seq_len * (in_dtype == RLS_BF16 ? 2 : 4);
+  const int pdl = pdl_mode(s, {{rewards, mb}, {values, mb}, {mask, mb}});
+  const int64_t M = num_envs * seq_len;
   if (in_dtype == RLS_F32)
-    gae_obs_skip_kernel<float><<<(unsigned)blocks, kSkipWarps * 32, 0, s>>>(
-        (const float*)rewards, (const float*)values, (const float*)mask, advantages, returns, num_envs, seq_len,
-        gamma, gl);
-  else
-    gae_obs_skip_kernel<__nv_bfloat16><<<(unsigned)blocks, kSkipWarps * 32, 0, s>>>(
-        (const __nv_bfloat16*)rewards, (const __nv_bfloat16*)values, (const __nv_bfloat16*)mask, advantages, returns,
-        num_envs, seq_len, gamma, gl);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+    return launch_rowk(gae_obs_skip_kernel<float>, blocks, kSkipWarps * 32, s, pdl, M, advantages, returns,
+                       (const float*)rewards, (const float*)values, (const float*)mask, advantages, returns, num_envs,
+                       seq_len, gamma, gl, pdl);
+  return launch_rowk(gae_obs_skip_kernel<__nv_bfloat16>, blocks, kSkipWarps * 32, s, pdl, M, advantages, returns,
+                     (const __nv_bfloat16*)rewards, (const __nv_bfloat16*)values, (const __nv_bfloat16*)mask,
+                     advantages, returns, num_envs, seq_len, gamma, gl, pdl);
 }
