@@ -152,3 +152,30 @@ def test_gae_obs_skip(n, t, dtype):
     np.testing.assert_allclose(rets.cpu().numpy(), wr, rtol=RTOL, atol=ATOL)
     if n * t <= 64 * 333:
         np.testing.assert_allclose(adv.cpu().numpy(), _compacted(rq, vq, m, 0.99, 0.95), rtol=1e-4, atol=1e-4)
+
+
+def test_fused_outputs_feed_the_next_calls():
+    """Each fused call's outputs read by the next call on the same stream (the
+    launches overlap under programmatic dependent launch, so a reader of the
+    previous launch's output must wait for it): normalised advantages -> their
+    discounted sums; returns -> observation-skip GAE; its advantages -> value
+    loss targets."""
+    _cuda()
+    import rl_triton
+    x = _inputs(1024, 256, 77)
+    r, v, term = D(x["r"]), D(x["v"]), D(x["term"])
+    mask = D((x["term"] == 0).astype(np.float32))
+    for _ in range(2):
+        norm, rets = rl_triton.compute_gae_normalized(r, v, term, return_returns=True)
+        disc = rl_triton.compute_discounted_returns(norm, term, gamma=0.9)
+        a2, _ = rl_triton.compute_gae_obs_skip(rets, v, mask, gamma=0.99, lambda_=0.95)
+        _, _, vl = rl_triton.compute_gae_value_loss(a2, v, term, rets)
+    wn, wr = _want(orc.gae(x["r"], x["v"], x["term"]), x["v"], 1e-8)
+    wn32, wr32 = wn.astype(np.float32), wr.astype(np.float32)
+    res = orc.compare(disc.cpu().numpy(), lambda p: orc.discounted_returns(wn32, x["term"], gamma=0.9, precision=p))
+    assert res["ok"], res
+    wa2, _ = orc.gae_obs_skip(wr32, x["v"], (x["term"] == 0).astype(np.float32), 0.99, 0.95)
+    np.testing.assert_allclose(a2.cpu().numpy(), wa2, rtol=1e-4, atol=1e-4)
+    adv3 = orc.gae(a2.cpu().numpy(), x["v"], x["term"])
+    want_loss = np.mean((rets.cpu().numpy().astype(np.float64) - (adv3 + x["v"])) ** 2)
+    np.testing.assert_allclose(float(vl), want_loss, rtol=1e-4)
