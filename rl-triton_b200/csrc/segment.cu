@@ -152,15 +152,19 @@ __global__ void __launch_bounds__(128) segment_walk(const SegArgs a) {
   }
 }
 
-constexpr int kBlockWalk = 512;   // threads of the block-per-row walk
-constexpr int kBlockElems = 4;    // consecutive (walk-order) elements per thread
+constexpr int kBlockWalk = 512;   // threads of the virtual-row fix-up block
+constexpr int kBlockElems = 4;    // consecutive (walk-order) elements per thread there
+// The time-split walks (one block per row): 8192 steps per pass, so the walk
+// to the first reset of a 1e-4 done rate takes one or two passes.
+constexpr int kSegWalk = 1024;
+constexpr int kSegElems = 8;
 
 // Block-per-row version of segment_walk (same results up to the rounding of
 // the decay products).
 template <int MODE>
-__global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a) {
-  constexpr int NW = kBlockWalk / 32;
-  constexpr int STEP = kBlockWalk * kBlockElems;
+__global__ void __launch_bounds__(kSegWalk) segment_walk_block(const SegArgs a) {
+  constexpr int NW = kSegWalk / 32;
+  constexpr int STEP = kSegWalk * kSegElems;
   __shared__ float s_w[NW];
   __shared__ float s_base;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -174,17 +178,17 @@ __global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a
   float base = 1.f;  // product of b over all earlier steps
   bool zero = (MODE == 0) && a.global_edge;
   for (int64_t k0 = 0; k0 < S && !zero; k0 += STEP) {
-    float b[kBlockElems];
-    int64_t col[kBlockElems];
+    float b[kSegElems];
+    int64_t col[kSegElems];
 #pragma unroll
-    for (int q = 0; q < kBlockElems; ++q) {
-      const int64_t k = k0 + (int64_t)threadIdx.x * kBlockElems + q;
+    for (int q = 0; q < kSegElems; ++q) {
+      const int64_t k = k0 + (int64_t)threadIdx.x * kSegElems + q;
       col[q] = k < S ? (a.backward ? (S - 1 - k) : k) : -1;
       b[q] = col[q] >= 0 ? ((a.exclusive && k == 0) ? 1.f : decay_at(a, row, col[q])) : 1.f;
     }
     float mine = 1.f;
 #pragma unroll
-    for (int q = 0; q < kBlockElems; ++q) mine *= b[q];
+    for (int q = 0; q < kSegElems; ++q) mine *= b[q];
     float incl = mine;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -202,7 +206,7 @@ __global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a
     float P = base * before * (lane == 0 ? 1.f : excl);
     if (MODE == 1) {
 #pragma unroll
-      for (int q = 0; q < kBlockElems; ++q) {
+      for (int q = 0; q < kSegElems; ++q) {
         P *= b[q];
         if (col[q] >= 0 && P != 0.f) {
           float* o = a.out + row * S + col[q];
@@ -228,7 +232,7 @@ __global__ void __launch_bounds__(kBlockWalk) segment_walk_block(const SegArgs a
 template <int MODE>
 int launch_walk(const SegArgs& a, void* stream) {
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (a.N <= 64) segment_walk_block<MODE><<<(unsigned)a.N, kBlockWalk, 0, s>>>(a);
+  if (a.N <= 64) segment_walk_block<MODE><<<(unsigned)a.N, kSegWalk, 0, s>>>(a);
   else segment_walk<MODE><<<(unsigned)((a.N + 3) / 4), 128, 0, s>>>(a);
   return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
 }
