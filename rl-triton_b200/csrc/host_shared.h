@@ -31,6 +31,7 @@ struct PdlIn {
 };
 int pdl_mode(cudaStream_t s, std::initializer_list<PdlIn> ins);
 void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes);
+void pdl_record(cudaStream_t s, std::initializer_list<PdlIn> outs);  // up to 4 ranges
 
 // Launch a kernel that triggers its dependents early: plainly when pdl_flag is
 // 0, else with the programmatic-stream-serialization attribute; either way its

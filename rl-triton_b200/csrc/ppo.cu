@@ -40,6 +40,8 @@ struct NormArgs {
   const void* values;   // V, for the returns
   int bf16;
   double2* partials;    // per CTA (sum, sum of squares)
+  unsigned* counter;    // CTAs done with pass 1 (the last one resets it)
+  float* mean_den;      // pass 1's last CTA: {mean, std + eps}
   float eps;
 };
 
@@ -123,7 +125,7 @@ __device__ void finish_stats(const double2* partials, int n, int64_t count, floa
 // may be the predecessor's output, Geom::pdl == 1).
 template <class P>
 __global__ void __launch_bounds__(kNormWarps * 32) gae_stats_kernel(const typename P::Params p, const Geom g,
-                                                                     float* tmp, double2* partials) {
+                                                                     float* tmp, NormArgs na) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t S = g.S;
   const int64_t W = (int64_t)gridDim.x * kNormWarps;
@@ -144,33 +146,37 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_stats_kernel(const typena
   }
   const double2 part = block_sum2<kNormWarps * 32>(s1, s2);
   pdl_wait();  // also in CTAs that stored nothing: the partials follow the predecessor
-  if (threadIdx.x == 0) partials[blockIdx.x] = part;
-}
-
-// Pass 2: every CTA reduces the partials in the same fixed order (identical
-// mean and std everywhere), then normalises its float4 groups of `tmp` (which
-// may be `norm` itself) and writes the returns.  Waits for pass 1 first.
-__global__ void __launch_bounds__(kStatThreads) norm_finish_kernel(const float* tmp, int64_t M,
-                                                                   const double2* partials, int nparts, NormArgs na) {
-  // Trigger only after the wait: a dependent then starts after pass 1 has
-  // completed, so it may read the raw advantages pass 1 wrote.
-  pdl_wait();
-  pdl_trigger();
-  __shared__ float s_mean, s_den;
-  {
+  // The last CTA to finish reduces the partials (fixed order) once for pass 2.
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    na.partials[blockIdx.x] = part;
+    __threadfence();
+    s_last = atomicAdd(na.counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
     float m, d, sd;
-    finish_stats<kStatThreads>(partials, nparts, M, na.eps, &m, &d, &sd);
+    finish_stats<kNormWarps * 32>(na.partials, gridDim.x, g.M, na.eps, &m, &d, &sd);
     if (threadIdx.x == 0) {
-      s_mean = m;
-      s_den = d;
-      if (blockIdx.x == 0 && na.stats) {
+      na.mean_den[0] = m;
+      na.mean_den[1] = d;
+      if (na.stats) {
         na.stats[0] = m;
         na.stats[1] = sd;
       }
+      *na.counter = 0u;
     }
   }
-  __syncthreads();
-  const float mean = s_mean, den = s_den;
+}
+
+// Pass 2: the normalised advantages and the returns, one float4 group per
+// thread per step, from the mean and std pass 1's last CTA left.  `tmp` may be
+// `norm` itself.  Waits for pass 1, then lets its own dependents start.
+__global__ void __launch_bounds__(kStatThreads) norm_finish_kernel(const float* tmp, int64_t M, NormArgs na) {
+  pdl_wait();
+  pdl_trigger();
+  const float mean = __ldcg(na.mean_den), den = __ldcg(na.mean_den + 1);
   const int64_t M4 = M / 4;  // rows are a multiple of 4 steps on this path
   const int64_t stride = (int64_t)gridDim.x * kStatThreads;
   for (int64_t gi = (int64_t)blockIdx.x * kStatThreads + threadIdx.x; gi < M4; gi += stride) {
@@ -285,6 +291,8 @@ struct ValueArgs {
   const void* values;    // V
   int bf16;
   double* partials;      // per CTA loss sums
+  unsigned* counter;     // CTAs done (the last one resets it)
+  float* loss;           // written by the last CTA
   int huber;
   float delta;
   float inv_count;
@@ -334,7 +342,24 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_value_kernel(const typena
   }
   const double2 t = block_sum2<kNormWarps * 32>(acc, 0.0);
   pdl_wait();  // also in CTAs that stored nothing
-  if (threadIdx.x == 0) va.partials[blockIdx.x] = t.x;
+  // The last CTA to finish sums the partials in a fixed order into the loss.
+  __shared__ int s_last;
+  if (threadIdx.x == 0) {
+    va.partials[blockIdx.x] = t.x;
+    __threadfence();
+    s_last = atomicAdd(va.counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence();
+    double a = 0.0;
+    for (int i = threadIdx.x; i < (int)gridDim.x; i += kNormWarps * 32) a += __ldcg(va.partials + i);
+    const double2 tot = block_sum2<kNormWarps * 32>(a, 0.0);
+    if (threadIdx.x == 0) {
+      *va.loss = (float)(tot.x * (double)va.inv_count);
+      *va.counter = 0u;
+    }
+  }
 }
 
 // Rows that do not start 16-byte aligned: GAE first, then this elementwise pass.
@@ -397,15 +422,13 @@ int launch_gae_norm(const typename P::Params& p, Geom g, NormArgs na, size_t ws_
   const size_t mb = (size_t)g.M * (na.bf16 ? 2 : 4);
   g.pdl = pdl_mode(s, {{p.r, mb}, {p.v, mb}, {p.term, mb}, {p.trunc, mb}, {p.boot, mb},
                        {p.boot_row, (size_t)g.N * 4}});
-  int st = launch_rowk(gae_stats_kernel<P>, blocks, kNormWarps * 32, s, g.pdl, g.M, tmp, nullptr, p, g, tmp,
-                       na.partials);
+  int st = launch_rowk(gae_stats_kernel<P>, blocks, kNormWarps * 32, s, g.pdl, g.M, tmp, nullptr, p, g, tmp, na);
   if (st) return st;
   const int64_t groups = g.M / 4;
-  int64_t fb = (groups + kStatThreads * 4 - 1) / (kStatThreads * 4);
-  if (fb > 2LL * sms) fb = 2LL * sms;
+  int64_t fb = (groups + kStatThreads - 1) / kStatThreads;
+  if (fb > 8LL * sms) fb = 8LL * sms;
   if (fb < 1) fb = 1;
-  return launch_rowk(norm_finish_kernel, fb, kStatThreads, s, 1, g.M, na.norm, na.rets, (const float*)tmp, g.M,
-                     (const double2*)na.partials, (int)blocks, na);
+  return launch_rowk(norm_finish_kernel, fb, kStatThreads, s, 1, g.M, na.norm, na.rets, (const float*)tmp, g.M, na);
 }
 
 template <class T>
@@ -457,6 +480,8 @@ extern "C" int rls_gae_normalized(const void* rewards, const void* values, const
   na.values = values;
   na.bf16 = in_dtype == RLS_BF16;
   na.partials = reinterpret_cast<double2*>(static_cast<char*>(ws) + 64);
+  na.counter = &reinterpret_cast<WsHeader*>(ws)->pad[0];
+  na.mean_den = reinterpret_cast<float*>(&reinterpret_cast<WsHeader*>(ws)->pad[2]);
   na.eps = eps;
 
 #define NORM_PARAMS(T)                                                                                    \
@@ -513,10 +538,13 @@ int launch_gae_value(const typename P::Params& p, const Geom& g, ValueArgs va, f
   Geom g2 = g;
   g2.pdl = pdl_mode(s, {{p.r, mb}, {p.v, mb}, {p.term, mb}, {p.trunc, mb}, {p.boot, mb},
                         {p.boot_row, (size_t)g.N * 4}, {va.new_v, (size_t)g.M * 4}});
+  va.loss = loss;
   int st = launch_rowk(gae_value_kernel<P>, blocks, kNormWarps * 32, s, g2.pdl, g.M, va.grad, va.rets, p, g2, va);
   if (st) return st;
-  return launch_rowk(value_loss_finish, 1, kStatThreads, s, 1, 1, loss, nullptr, (const double*)va.partials,
-                     (int)blocks, va.inv_count, loss);
+  // It triggers its dependents at once: all four outputs are the stream's record.
+  const size_t ob = (size_t)g.M * 4;
+  pdl_record(s, {{va.grad, ob}, {va.rets, ob}, {va.adv, ob}, {loss, 4}});
+  return RLS_OK;
 }
 
 template <class T>
@@ -571,6 +599,8 @@ extern "C" int rls_gae_value_loss(const void* rewards, const void* values, const
   va.values = values;
   va.bf16 = in_dtype == RLS_BF16;
   va.partials = reinterpret_cast<double*>(static_cast<char*>(ws) + 64);
+  va.counter = &reinterpret_cast<WsHeader*>(ws)->pad[0];
+  va.loss = loss;
   va.huber = loss_kind == RLS_LOSS_HUBER;
   va.delta = delta;
   va.inv_count = (float)(1.0 / (double)g.M);

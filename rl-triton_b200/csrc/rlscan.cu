@@ -73,7 +73,7 @@ struct PdlRange {
 };
 struct PdlRecord {
   cudaStream_t s;
-  PdlRange out[2];
+  PdlRange out[4];
   bool used;
 };
 static PdlRecord g_pdl[64];
@@ -99,7 +99,7 @@ int pdl_mode(cudaStream_t s, std::initializer_list<PdlIn> ins) {
   return 2;
 }
 
-void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes) {
+void pdl_record(cudaStream_t s, std::initializer_list<PdlIn> outs) {
   PdlRecord* r = pdl_find(s);
   if (!r) {
     r = &g_pdl[g_pdl_next];
@@ -107,8 +107,16 @@ void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes
     r->s = s;
     r->used = true;
   }
-  r->out[0] = PdlRange{(uintptr_t)out0, out0 ? (uintptr_t)out0 + bytes : 0};
-  r->out[1] = PdlRange{(uintptr_t)out1, out1 ? (uintptr_t)out1 + bytes : 0};
+  int k = 0;
+  for (const PdlIn& o : outs) {
+    if (k == 4) break;
+    r->out[k++] = PdlRange{(uintptr_t)o.p, o.p ? (uintptr_t)o.p + o.bytes : 0};
+  }
+  for (; k < 4; ++k) r->out[k] = PdlRange{0, 0};
+}
+
+void pdl_record(cudaStream_t s, const void* out0, const void* out1, size_t bytes) {
+  pdl_record(s, {{out0, bytes}, {out1, bytes}});
 }
 
 }  // namespace rls
