@@ -60,21 +60,28 @@ __device__ __forceinline__ void walk_row(const typename P::Params& p, const Geom
   const int64_t S = g.S, rbase = row * S;
   const int64_t nch = (S + CH - 1) / CH;
   auto cb_of = [&](int64_t k) { return (nch - 1 - k) * CH; };
-  Rows2Chunk<P, 1> ch[2];
+  // Two named chunk buffers (an array indexed by k & 1 would live in local memory).
+  Rows2Chunk<P, 1> a, b;
   typename P::Nbr edge_nbr{};
   float carry = 0.f;
-  rows2_load<P, 1>(p, rbase, S, cb_of(0), lane, ch[0]);
-  for (int64_t k = 0; k < nch; ++k) {
-    if (k + 1 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 1), lane, ch[(k + 1) & 1]);
+  auto chunk = [&](int64_t k, const Rows2Chunk<P, 1>& ch) {
     ChunkScan<P, 1> cs;
     cs.col0[0] = cb_of(k) + lane * VEC;
     cs.row[0] = row;
     cs.i0[0] = rbase + cs.col0[0];
     cs.valid[0] = cs.col0[0] < S;
     cs.edge_v[0] = cs.valid[0] && (cs.col0[0] + VEC == S);
-    edge_nbr = cs.pass1(p, g, lane, ch[k & 1], edge_nbr);
+    edge_nbr = cs.pass1(p, g, lane, ch, edge_nbr);
     const int64_t col0 = cs.col0[0];
-    carry = cs.pass2(p, g, ch[k & 1], carry, [&](int, int q, float4 v0, float4) { sink(col0 + q, v0); });
+    carry = cs.pass2(p, g, ch, carry, [&](int, int q, float4 v0, float4) { sink(col0 + q, v0); });
+  };
+  rows2_load<P, 1>(p, rbase, S, cb_of(0), lane, a);
+  for (int64_t k = 0; k < nch; k += 2) {
+    if (k + 1 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 1), lane, b);
+    chunk(k, a);
+    if (k + 1 >= nch) break;
+    if (k + 2 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 2), lane, a);
+    chunk(k + 1, b);
   }
 }
 
@@ -415,6 +422,9 @@ int launch_gae_norm(const typename P::Params& p, Geom g, NormArgs na, size_t ws_
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
   const int sms = num_sms_of(dev);
+  // One warp per row: too few rows to fill the GPU take the GAE kernel choice
+  // (virtual rows, look-back) and the separate statistics passes instead.
+  if (g.N < 8LL * sms) return RLS_EUNSUPPORTED;
   int64_t blocks = (g.N + kNormWarps - 1) / kNormWarps;
   if (blocks > 8LL * sms) blocks = 8LL * sms;
   if ((size_t)64 + (size_t)blocks * sizeof(double2) > ws_bytes) return RLS_EWORKSPACE;
@@ -504,8 +514,9 @@ extern "C" int rls_gae_normalized(const void* rewards, const void* values, const
 #undef NORM_PARAMS
   if (st != RLS_EUNSUPPORTED) return st;
 
-  // Rows that do not start 16-byte aligned: GAE into the advantages (or the
-  // output as scratch), then a statistics pass and a normalise pass.
+  // Rows that do not start 16-byte aligned, or too few rows for one warp per
+  // row: GAE into the advantages (or the output as scratch), then a statistics
+  // pass and a normalise pass.
   float* adv = advantages ? advantages : normalized;
   int cur = 0;
   if (cudaGetDevice(&cur) != cudaSuccess) return RLS_ECUDA;
@@ -530,6 +541,7 @@ int launch_gae_value(const typename P::Params& p, const Geom& g, ValueArgs va, f
   if (g.S % VEC != 0) return RLS_EUNSUPPORTED;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return RLS_ECUDA;
+  if (g.N < 8LL * num_sms_of(dev)) return RLS_EUNSUPPORTED;  // few rows: GAE's own kernel choice, then the loss pass
   int64_t blocks = (g.N + kNormWarps - 1) / kNormWarps;
   const int64_t cap = (int64_t)8 * num_sms_of(dev);
   if (blocks > cap) blocks = cap;
@@ -621,8 +633,8 @@ extern "C" int rls_gae_value_loss(const void* rewards, const void* values, const
   }
 #undef VAL_PARAMS
   if (st != RLS_EUNSUPPORTED) return st;
-  // Unaligned rows: GAE into the advantages (the gradient buffer as scratch),
-  // then the elementwise loss pass.
+  // Unaligned rows, or too few rows for one warp per row: GAE into the
+  // advantages (the gradient buffer as scratch), then the elementwise loss pass.
   float* adv = advantages ? advantages : grad;
   st = rls_gae(rewards, values, terminateds, truncateds, bootstrap, boot_kind, adv, num_envs, seq_len, gamma,
                lambda_, in_dtype, nullptr, ws, ws_bytes, stream);
