@@ -173,11 +173,11 @@ int launch_r(const typename Alg::Params& p, Geom g, void* ws, size_t ws_bytes, c
 constexpr int kRowWarps = 4;  // rows (warps) per CTA of the row kernel
 
 
-// The row kernel needs every row to start on a 16-byte boundary; other shapes
-// fall back to the flat look-back kernel.
+// The first row kernel takes any row length (per-element accesses when rows do
+// not start 16-byte aligned).
 template <class Alg>
-bool use_rows(const Geom& g) {
-  return g.S % Alg::kVec == 0;
+bool use_rows(const Geom&) {
+  return true;  // any length: unaligned rows take per-element accesses
 }
 
 template <class Alg, int R>
@@ -637,6 +637,7 @@ int family(const Geom& g) {
   if (m == 8) return rows_ok ? 8 : 3;
   if (m != 0) return 0;
   if (rows_ok && g.N >= kRowsMinEnvs) return 4;
+  if (g.N >= kRowsMinEnvs) return 0;  // many unaligned rows: the first row kernel, per-element accesses
   return rows_ok ? 8 : 3;  // virtual rows where the policy and the length allow, else flat3
 }
 

@@ -17,8 +17,9 @@
 // streaming stores.  The element rules (coefficients, edges, emitted outputs)
 // are the same policies the flat look-back kernel uses (algs.cuh).
 //
-// Requirement: seq_len % VEC == 0, so every row starts on a 16-byte boundary
-// (checked by the dispatcher; other shapes use the flat kernel).
+// Rows whose length is a multiple of VEC start on a 16-byte boundary and use
+// 16-byte vector accesses; other lengths take per-element accesses (the rows
+// then start anywhere), with the same per-element row-end handling.
 #pragma once
 #include "algs.cuh"
 
@@ -42,6 +43,9 @@ rows_kernel(const typename Alg::Params p, const Geom g) {
   const int64_t rend = rbase + S;
   const int64_t nch = (S + CH - 1) / CH;
   const bool glob = g.edge_global != 0;
+  // Rows of a length that is not a multiple of VEC do not start 16-byte
+  // aligned: every access is then per element (coalesced across the warp).
+  const bool vec_ok = (S % VEC) == 0;
 
   float carry = 0.f;  // state entering the chunk (edges fold the boundary in)
   Nbr edge_nbr{};     // neighbour across the chunk edge, from the previous chunk
@@ -57,7 +61,7 @@ rows_kernel(const typename Alg::Params p, const Geom g) {
     for (int r = 0; r < ROUNDS; ++r) {
       const int64_t col = cbase + r * RUN + lane * VEC;
       const int64_t i = rbase + col;
-      if (col + VEC <= S) Alg::load(p, i, rend, true, run[r], nullptr, 0);
+      if (vec_ok && col + VEC <= S) Alg::load(p, i, rend, true, run[r], nullptr, 0);
       else Alg::load(p, i, rend, false, run[r], nullptr, 0);
     }
     if (g.pdl == 2 && k == 0) pdl_wait();  // the first loads are in flight; no store before this
@@ -203,7 +207,7 @@ rows_kernel(const typename Alg::Params p, const Geom g) {
         }
       }
       if (col0 < S) {
-        const bool full = col0 + VEC <= S;
+        const bool full = vec_ok && col0 + VEC <= S;
         store_run<VEC>(p.out0, rbase + col0, rend, full, o0);
         if constexpr (Alg::kOuts > 1) store_run<VEC>(p.out1, rbase + col0, rend, full, o1);
       }

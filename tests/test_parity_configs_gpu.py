@@ -128,3 +128,15 @@ def test_config5b_single_sequence_2pow28():
     del got
     got = rl_triton.compute_gae(x["r"], x["v"], x["term"], gamma=0.99, lambda_=0.95)
     _check(got, lambda p: orc.gae(h["r"], h["v"], h["term"], gamma=0.99, lam=0.95, precision=p), "cfg5b gae")
+
+
+def test_many_unaligned_rows_default_path():
+    """4096 rows of 131 steps (rows not 16-byte aligned: the first row kernel
+    with per-element accesses on the default path), all seven estimators."""
+    cfg, x, h = _inputs("unaligned")
+    calls = bench.make_calls(cfg, x)
+    for f, call in calls.items():
+        out = call()
+        outs = out if isinstance(out, tuple) else (out,)
+        for k, o in enumerate(outs):
+            _check(o, lambda p: bench.oracle_output(f, h, cfg, p)[k], f"unaligned {f}[{k}]")
