@@ -234,32 +234,36 @@ def gae_obs_skip(r, v, mask, gamma=1.0, lam=1.0, precision="f32", nthreads=None)
 
 
 def compare(got, oracle, rtol=1e-5, atol=1e-5):
-    """Parity verdict of a result against the oracle.
+    """Parity verdict of a result against the oracle, element by element.
 
-    `oracle(precision)` returns the oracle's output ("f32" or "f64").  The
-    result passes when it is within rtol / atol of the fp32 sequential oracle
-    (the reference's own fp32 loop order).  Only where the fp32 oracle is itself
-    off the fp64 oracle by more than that tolerance (long running sums, where
-    any reassociation differs by more than 1e-5) does it pass instead when its
-    worst error against fp64 is at most twice the fp32 oracle's plus atol.
-    Returns a dict: ok, max_abs_err (vs fp32 oracle), criterion, and, when the
-    fp64 leg ran, err_vs_f64 and oracle_f32_err_vs_f64."""
+    `oracle(precision)` returns the oracle's output ("f32" or "f64").  An
+    element passes when it is within rtol / atol of the fp32 sequential oracle
+    (the reference's own fp32 loop order), or within rtol / atol of the fp64
+    oracle (the exact answer), or -- where the fp32 oracle itself is off the
+    exact answer (long running sums, values that end near zero after large
+    intermediates) -- when its distance to the fp64 oracle is at most twice the
+    fp32 oracle's own distance there, plus atol.  Where the fp32 oracle is
+    exact to within atol the last rule is the tolerance itself.  Returns a dict:
+    ok, max_abs_err (vs fp32 oracle), criterion, and, when the fp64 leg ran,
+    err_vs_f64, oracle_f32_err_vs_f64 and how many elements needed each rule."""
     got = np.asarray(got, dtype=np.float64)
     w32 = np.asarray(oracle("f32"), dtype=np.float64)
     diff = np.abs(got - w32)
     res = {"max_abs_err": float(diff.max()) if diff.size else 0.0, "rtol": rtol, "atol": atol}
-    if not diff.size or bool(np.all(diff <= atol + rtol * np.abs(w32))):
+    pass32 = diff <= atol + rtol * np.abs(w32)
+    if not diff.size or bool(np.all(pass32)):
         res.update(ok=True, criterion="fp32 oracle within rtol/atol")
         return res
     w64 = np.asarray(oracle("f64"), dtype=np.float64)
-    ours = float(np.max(np.abs(got - w64)))
+    d64 = np.abs(got - w64)
     ref_dev = np.abs(w32 - w64)
-    ref = float(ref_dev.max())
-    ref_outside = bool(np.any(ref_dev > atol + rtol * np.abs(w64)))
-    res.update(err_vs_f64=ours, oracle_f32_err_vs_f64=ref)
-    if ref_outside:
-        res.update(ok=ours <= 2 * ref + atol, criterion="fp32 oracle itself outside tolerance of fp64: "
-                                                        "error vs fp64 <= 2x the fp32 oracle's + atol")
-    else:
-        res.update(ok=False, criterion="fp32 oracle within tolerance of fp64, result is not")
+    pass64 = d64 <= atol + rtol * np.abs(w64)
+    pass_ref = d64 <= 2 * ref_dev + atol
+    ok = pass32 | pass64 | pass_ref
+    res.update(ok=bool(np.all(ok)), err_vs_f64=float(d64.max()), oracle_f32_err_vs_f64=float(ref_dev.max()),
+               elements_outside_fp32_tol=int((~pass32).sum()),
+               of_which_within_fp64_tol=int((~pass32 & pass64).sum()),
+               of_which_within_2x_fp32_oracle_error=int((~pass32 & ~pass64 & pass_ref).sum()),
+               criterion="per element: fp32 oracle within rtol/atol, or fp64 oracle within rtol/atol, or "
+                         "distance to fp64 <= 2x the fp32 oracle's own + atol")
     return res

@@ -52,19 +52,12 @@ def _whole(alg, x, precision="f32"):
 
 
 def _close(got, alg, x, rtol=RTOL, atol=ATOL):
-    """Within rtol / atol of the fp32 sequential oracle -- or, where splitting the
-    sequence reassociates a long fp32 running sum (an episodic prefix sum over
-    10^4-step episodes), no less accurate than the fp32 sequential reference
-    itself: the worst error against the fp64 oracle at most twice the
-    reference's own worst error (plus atol)."""
-    w32 = _whole(alg, x)
-    err32 = np.abs(got - w32)
-    if (err32 <= atol + rtol * np.abs(w32)).all():
-        return
-    w64 = _whole(alg, x, "f64")
-    ours, ref = float(np.max(np.abs(got - w64))), float(np.max(np.abs(w32 - w64)))
-    assert ours <= 2 * ref + atol, (f"{alg}: max |got - f32 oracle| = {float(err32.max())}, max error vs fp64 "
-                                    f"{ours} vs the fp32 reference's {ref}")
+    """oracle.compare against the oracle on the whole sequence (element-wise:
+    within rtol / atol of the fp32 or the fp64 oracle, or -- where splitting the
+    sequence reassociates a long fp32 running sum -- no further from fp64 than
+    twice the fp32 oracle's own error, plus atol)."""
+    res = orc.compare(got, lambda p: _whole(alg, x, p), rtol, atol)
+    assert res["ok"], f"{alg}: {res}"
 
 
 def _segment_call(alg, x, rank, world, to, **kw):
