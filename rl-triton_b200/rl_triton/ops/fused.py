@@ -131,6 +131,32 @@ def compute_gae_obs_skip(
         f"rewards {rewards.shape}, values {values.shape} and response_mask {response_mask.shape} must match"
     _placed(rewards, values, response_mask)
     mask = response_mask if response_mask.dtype in (torch.float32, torch.bfloat16) else response_mask.float()
-    adv, rets = nat.ops.gae_obs_skip(rewards, values, mask, float(gamma), float(lambda_))
+    num_envs, seq_len = rewards.shape
+    if num_envs < _OBS_SKIP_MIN_ROWS and seq_len >= _OBS_SKIP_LONG_ROW:
+        adv, rets = _obs_skip_long_rows(rewards, values, mask, float(gamma), float(lambda_))
+    else:
+        adv, rets = nat.ops.gae_obs_skip(rewards, values, mask, float(gamma), float(lambda_))
     _done(rewards)
     return (adv, rets) if return_returns else adv
+
+
+# The fused kernel gives each row one warp: a handful of very long rows (a few
+# sequences of 10^5+ tokens) would leave the GPU idle.  They take the two scans
+# as generic affine scans instead, which split rows across the whole GPU.
+_OBS_SKIP_MIN_ROWS = 8 * 148
+_OBS_SKIP_LONG_ROW = 4096
+
+
+def _obs_skip_long_rows(rewards, values, mask, gamma, lambda_):
+    from rl_triton.ops._scan import _affine
+
+    r, v, m = rewards.float(), values.float(), mask.float()
+    # NV[t] = m[t+1] V[t+1] + (1 - m[t+1]) NV[t+1], NV[T-1] = 0
+    m_next = torch.nn.functional.pad(m[:, 1:], (0, 1))
+    v_next = torch.nn.functional.pad(v[:, 1:], (0, 1))
+    nv = _affine((m_next * v_next).contiguous(), (1.0 - m_next).contiguous(), None, 0)
+    # A[t] = m[t] (r + gamma NV - V) + (m[t] gamma lambda + 1 - m[t]) A[t+1], A[T] = 0
+    u = m * (r + gamma * nv - v)
+    b = m * (gamma * lambda_) + (1.0 - m)
+    adv = _affine(u.contiguous(), b.contiguous(), None, 0)
+    return adv, adv + v

@@ -179,3 +179,20 @@ def test_fused_outputs_feed_the_next_calls():
     adv3 = orc.gae(a2.cpu().numpy(), x["v"], x["term"])
     want_loss = np.mean((rets.cpu().numpy().astype(np.float64) - (adv3 + x["v"])) ** 2)
     np.testing.assert_allclose(float(vl), want_loss, rtol=1e-4)
+
+
+def test_gae_obs_skip_few_long_rows():
+    """A few very long rows take the two generic affine scans (split across the
+    whole GPU) instead of one warp per row."""
+    _cuda()
+    import rl_triton
+    g = np.random.default_rng(3)
+    n, t = 2, 300000
+    r = g.standard_normal((n, t)).astype(np.float32)
+    v = g.standard_normal((n, t)).astype(np.float32)
+    m = (np.cumsum(g.random((n, t)) < 1e-3, axis=1) % 2 == 0).astype(np.float32)
+    adv, rets = rl_triton.compute_gae_obs_skip(D(r), D(v), D(m), gamma=0.999, lambda_=0.95)
+    res = orc.compare(adv.cpu().numpy(), lambda p: orc.gae_obs_skip(r, v, m, 0.999, 0.95, precision=p)[0], RTOL, ATOL)
+    assert res["ok"], res
+    res = orc.compare(rets.cpu().numpy(), lambda p: orc.gae_obs_skip(r, v, m, 0.999, 0.95, precision=p)[1], RTOL, ATOL)
+    assert res["ok"], res
