@@ -55,7 +55,7 @@ def _close(got, alg, x, rtol=RTOL, atol=ATOL):
     """oracle.compare against the oracle on the whole sequence (element-wise:
     within rtol / atol of the fp32 or the fp64 oracle, or -- where splitting the
     sequence reassociates a long fp32 running sum -- no further from fp64 than
-    twice the fp32 oracle's own error, plus atol)."""
+    twice the fp32 oracle's worst error, plus atol)."""
     res = orc.compare(got, lambda p: _whole(alg, x, p), rtol, atol)
     assert res["ok"], f"{alg}: {res}"
 

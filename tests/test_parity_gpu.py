@@ -343,7 +343,7 @@ def _no_less_accurate(got, oracle, msg):
     this repository uses): within rtol / atol of the fp32 sequential oracle, or
     of the fp64 oracle, or -- where cutting a running sum over 10^4-10^5-step
     episodes reassociates it -- no further from fp64 than twice the fp32
-    oracle's own error there, plus atol."""
+    oracle's worst error, plus atol."""
     res = orc.compare(got, oracle, RTOL, ATOL)
     assert res["ok"], f"{msg}: {res}"
 
