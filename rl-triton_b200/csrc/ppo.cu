@@ -52,7 +52,8 @@ __device__ __forceinline__ float load_value(const void* p, int bf16, int64_t i) 
 
 // Walk one row from the window end (backward), chunk by chunk with the next
 // chunk's loads in flight, handing each emitted vector to `sink(col, v)`.
-template <class P, class Sink>
+// SINGLE: the row is one chunk (seq_len <= 32 x VEC): one buffer, no loop.
+template <class P, bool SINGLE, class Sink>
 __device__ __forceinline__ void walk_row(const typename P::Params& p, const Geom& g, int64_t row, int lane,
                                          Sink&& sink) {
   constexpr int VEC = Rows2Chunk<P, 1>::VEC;
@@ -61,7 +62,7 @@ __device__ __forceinline__ void walk_row(const typename P::Params& p, const Geom
   const int64_t nch = (S + CH - 1) / CH;
   auto cb_of = [&](int64_t k) { return (nch - 1 - k) * CH; };
   // Two named chunk buffers (an array indexed by k & 1 would live in local memory).
-  Rows2Chunk<P, 1> a, b;
+  Rows2Chunk<P, 1> a;
   typename P::Nbr edge_nbr{};
   float carry = 0.f;
   auto chunk = [&](int64_t k, const Rows2Chunk<P, 1>& ch) {
@@ -76,12 +77,17 @@ __device__ __forceinline__ void walk_row(const typename P::Params& p, const Geom
     carry = cs.pass2(p, g, ch, carry, [&](int, int q, float4 v0, float4) { sink(col0 + q, v0); });
   };
   rows2_load<P, 1>(p, rbase, S, cb_of(0), lane, a);
-  for (int64_t k = 0; k < nch; k += 2) {
-    if (k + 1 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 1), lane, b);
-    chunk(k, a);
-    if (k + 1 >= nch) break;
-    if (k + 2 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 2), lane, a);
-    chunk(k + 1, b);
+  if constexpr (SINGLE) {
+    chunk(0, a);
+  } else {
+    Rows2Chunk<P, 1> b;
+    for (int64_t k = 0; k < nch; k += 2) {
+      if (k + 1 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 1), lane, b);
+      chunk(k, a);
+      if (k + 1 >= nch) break;
+      if (k + 2 < nch) rows2_load<P, 1>(p, rbase, S, cb_of(k + 2), lane, a);
+      chunk(k + 1, b);
+    }
   }
 }
 
@@ -130,7 +136,7 @@ __device__ void finish_stats(const double2* partials, int n, int64_t count, floa
 // serialization: it triggers its dependents at once and waits for its
 // predecessor before its first store (and before its first load when an input
 // may be the predecessor's output, Geom::pdl == 1).
-template <class P>
+template <class P, bool SINGLE>
 __global__ void __launch_bounds__(kNormWarps * 32) gae_stats_kernel(const typename P::Params p, const Geom g,
                                                                      float* tmp, NormArgs na) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -141,7 +147,7 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_stats_kernel(const typena
   bool waited = g.pdl == 1;
   double s1 = 0.0, s2 = 0.0;
   for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < g.N; row += W) {
-    walk_row<P>(p, g, row, lane, [&](int64_t col, float4 v) {
+    walk_row<P, SINGLE>(p, g, row, lane, [&](int64_t col, float4 v) {
       if (!waited) {
         pdl_wait();
         waited = true;
@@ -305,7 +311,7 @@ struct ValueArgs {
   float inv_count;
 };
 
-template <class P>
+template <class P, bool SINGLE>
 __global__ void __launch_bounds__(kNormWarps * 32) gae_value_kernel(const typename P::Params p, const Geom g,
                                                                      const ValueArgs va) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -316,7 +322,7 @@ __global__ void __launch_bounds__(kNormWarps * 32) gae_value_kernel(const typena
   bool waited = g.pdl == 1;
   double acc = 0.0;
   for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < g.N; row += W) {
-    walk_row<P>(p, g, row, lane, [&](int64_t col, float4 a) {
+    walk_row<P, SINGLE>(p, g, row, lane, [&](int64_t col, float4 a) {
       if (!waited) {
         pdl_wait();
         waited = true;
@@ -432,7 +438,12 @@ int launch_gae_norm(const typename P::Params& p, Geom g, NormArgs na, size_t ws_
   const size_t mb = (size_t)g.M * (na.bf16 ? 2 : 4);
   g.pdl = pdl_mode(s, {{p.r, mb}, {p.v, mb}, {p.term, mb}, {p.trunc, mb}, {p.boot, mb},
                        {p.boot_row, (size_t)g.N * 4}});
-  int st = launch_rowk(gae_stats_kernel<P>, blocks, kNormWarps * 32, s, g.pdl, g.M, tmp, nullptr, p, g, tmp, na);
+  constexpr int64_t CH = 32 * VEC;
+  int st = g.S <= CH
+               ? launch_rowk(gae_stats_kernel<P, true>, blocks, kNormWarps * 32, s, g.pdl, g.M, tmp, nullptr, p, g,
+                             tmp, na)
+               : launch_rowk(gae_stats_kernel<P, false>, blocks, kNormWarps * 32, s, g.pdl, g.M, tmp, nullptr, p, g,
+                             tmp, na);
   if (st) return st;
   const int64_t groups = g.M / 4;
   int64_t fb = (groups + kStatThreads - 1) / kStatThreads;
@@ -551,7 +562,11 @@ int launch_gae_value(const typename P::Params& p, const Geom& g, ValueArgs va, f
   g2.pdl = pdl_mode(s, {{p.r, mb}, {p.v, mb}, {p.term, mb}, {p.trunc, mb}, {p.boot, mb},
                         {p.boot_row, (size_t)g.N * 4}, {va.new_v, (size_t)g.M * 4}});
   va.loss = loss;
-  int st = launch_rowk(gae_value_kernel<P>, blocks, kNormWarps * 32, s, g2.pdl, g.M, va.grad, va.rets, p, g2, va);
+  constexpr int64_t CH = 32 * VEC;
+  int st = g.S <= CH ? launch_rowk(gae_value_kernel<P, true>, blocks, kNormWarps * 32, s, g2.pdl, g.M, va.grad,
+                                   va.rets, p, g2, va)
+                     : launch_rowk(gae_value_kernel<P, false>, blocks, kNormWarps * 32, s, g2.pdl, g.M, va.grad,
+                                   va.rets, p, g2, va);
   if (st) return st;
   // It triggers its dependents at once: all four outputs are the stream's record.
   const size_t ob = (size_t)g.M * 4;
