@@ -528,6 +528,27 @@ def time_fused(sets, stream, use_graph, world, hbm):
         out[name] = {"us_per_call": r["us_per_launch"], "full_call_us": r["full_call_us"],
                      "frac_of_peak": round(alg / (r["us_per_launch"] * 1e-6) / 1e9 / hbm, 4)}
     out["speedup"] = round(out["composed"]["us_per_call"] / out["fused"]["us_per_call"], 3)
+
+    # GAE + returns + value loss and its gradient for the value head's outputs.
+    nvs = [(x["v"].float() + 0.1).requires_grad_(True) for x in sets]
+
+    def vl_fused(x, nv):
+        _, _, loss = rl_triton.compute_gae_value_loss(x["r"], x["v"], x["term"], nv, gamma=0.99, lambda_=0.95)
+        loss.backward()
+
+    def vl_composed(x, nv):
+        a = rl_triton.compute_gae(x["r"], x["v"], x["term"], gamma=0.99, lambda_=0.95)
+        loss = torch.nn.functional.mse_loss(nv, a + x["v"].float())
+        loss.backward()
+
+    vcalls = [{"fused": (lambda x=x, nv=nv: vl_fused(x, nv)), "composed": (lambda x=x, nv=nv: vl_composed(x, nv))}
+              for x, nv in zip(sets, nvs)]
+    vl = {"workload": "advantages, returns, value loss (MSE) and its gradient (backward)"}
+    for name in ("fused", "composed"):
+        r = time_function(vcalls, name, stream, False, fixed_reps=8 if world > 1 else 0)
+        vl[name] = {"full_call_us": r["full_call_us"]}
+    vl["speedup"] = round(vl["composed"]["full_call_us"] / vl["fused"]["full_call_us"], 3)
+    out["value_loss"] = vl
     return out
 
 
