@@ -735,8 +735,9 @@ const char* rls_status_string(int status) {
 }
 
 const char* rls_build_info(void) {
-  return "librlscan: sm_100a affine scans (single-pass decoupled look-back, 4 warps/CTA, "
-         "rounds 1/2/4, fp32 + bf16 inputs)";
+  return "librlscan: sm_100a affine scans (warp-per-row kernels with programmatic dependent launch, "
+         "virtual rows and decoupled look-back for long rows, bulk-copy tiles for unaligned rows; "
+         "fp32 + bf16 inputs, fp32 arithmetic)";
 }
 
 // ---------------------------------------------------------------------------
