@@ -64,8 +64,10 @@ int prepare_layout(void* ws, size_t wsb, int layout, cudaStream_t s) {
 // kernel waits (griddepcontrol.wait) for the preceding grid before its first
 // store, and before its first load unless none of its inputs can be an output
 // of the preceding library launch on the stream.  Only the row kernels trigger
-// their dependents early; any other preceding kernel (this library's or not)
-// completes before a dependent starts, so the overlap check needs only the
+// their dependents early across calls (the virtual-row scan and carry kernels
+// trigger too, but their dependents are the next kernels of the same call,
+// which wait before touching memory); any other preceding kernel (this
+// library's or not) completes before a dependent starts, so the overlap check needs only the
 // outputs of the last row-kernel launch per stream, kept here under the launch
 // lock.
 struct PdlRange {
@@ -452,6 +454,9 @@ namespace rls {
 int vrows_finish(int alg, const void* f0, const void* f1, int bf16, float* out, int64_t M, int64_t S, float coef,
                  int ends_at, float* seg_a, float* seg_b, float* carry, int* seg_code, int64_t nseg, int64_t L,
                  cudaStream_t s);
+int vrows_finish_vtrace(const void* lpt, const void* lpb, const void* term, const void* trunc, int bf16, float* out0,
+                        float* out1, int64_t M, int64_t S, float gamma, float rho_bar, float c_bar, float* seg_a,
+                        float* seg_b, float* carry, int* seg_code, int64_t nseg, int64_t L, cudaStream_t s);
 }  // namespace rls
 
 namespace {
@@ -495,6 +500,23 @@ struct VSpec<DiscountedT<T, TR, PB>> {
     return {RLS_ALG_DISCOUNTED, p.term, p.trunc, p.gamma, 0};
   }
 };
+// V-trace: two outputs and a per-step decay gamma * min(c_bar, ratio); the
+// fix-up (vrows_finish_vtrace) walks the decay product, bounded by gamma*c_bar.
+template <class T, bool TR, bool PB>
+struct VSpec<VtraceT<T, TR, PB>> {
+  static constexpr bool ok = true;
+  static VrowsSpec get(const typename VtraceT<T, TR, PB>::Params& p) {
+    return {-1, p.term, p.trunc, p.gamma * p.c_bar, 0};
+  }
+};
+template <class T>
+struct IsVtrace {
+  static constexpr bool value = false;
+};
+template <class T, bool TR, bool PB>
+struct IsVtrace<VtraceT<T, TR, PB>> {
+  static constexpr bool value = true;
+};
 template <class T, bool PREV>
 struct VSpec<ForwardT<T, PREV>> {
   static constexpr bool ok = true;
@@ -507,6 +529,7 @@ struct VSpec<ForwardT<T, PREV>> {
 
 constexpr int64_t kVrowsSegs = 32 * 148;  // segments if the occupancy query fails: 32 warps per SM
 constexpr int64_t kVrowsMinLen = 16384;   // auto: shortest segment worth its fix-up
+constexpr int64_t kVrowsMinLenVtrace = 1024;  // the same for V-trace (its fix-up reads the decay)
 
 // forced (RLS_PATH=vrows): any length; auto: only when segments reach
 // kVrowsMinLen.  Policies with other outputs fall back to flat3.
@@ -549,7 +572,14 @@ int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t ws
     // auto: the fix-up reaches up to -110 / ln(coef) steps into a segment (the
     // decay product underflows there); keep that under a quarter of it.
     int64_t min_len = kVrowsMinLen;
-    if (v.coef > 0.f && v.coef < 1.f) min_len = std::max(min_len, (int64_t)(4.0 * -110.0 / std::log((double)v.coef)));
+    if (IsVtrace<P>::value) {
+      // The fix-up walks to the first reset or until the product of the
+      // per-step c < 1 underflows (a few hundred steps at c_bar = 1); even a
+      // walk over a whole segment re-reads fewer bytes than the scan did.
+      min_len = kVrowsMinLenVtrace;
+    } else if (v.coef > 0.f && v.coef < 1.f) {
+      min_len = std::max(min_len, (int64_t)(4.0 * -110.0 / std::log((double)v.coef)));
+    }
     if ((!forced && L < min_len) || L > 0x7fffffffLL) return Flat3L<P>::run(p, g, ws, wsb, s);
     // The segment words live in the stream's workspace across three launches,
     // enqueued under the caller's launch lock.
@@ -559,6 +589,9 @@ int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t ws
     int* code = reinterpret_cast<int*>(carry + nseg);
     vseg_kernel<P><<<(unsigned)((nseg + 3) / 4), 128, 0, s>>>(p, g, L, nseg, v.coef, seg_a, seg_b, code);
     if (cudaPeekAtLastError() != cudaSuccess) return RLS_ECUDA;
+    if constexpr (IsVtrace<P>::value)
+      return vrows_finish_vtrace(p.lpt, p.lpb, p.term, p.trunc, sizeof(typename P::InT) == 2, p.out0, p.out1, g.M,
+                                 g.S, p.gamma, p.rho_bar, p.c_bar, seg_a, seg_b, carry, code, nseg, L, s);
     return vrows_finish(v.alg, v.f0, v.f1, sizeof(typename P::InT) == 2, p.out0, g.M, g.S, v.coef, v.ends_at, seg_a,
                         seg_b, carry, code, nseg, L, s);
   }

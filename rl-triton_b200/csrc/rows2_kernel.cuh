@@ -921,6 +921,9 @@ __global__ void __launch_bounds__(128) vseg_kernel(const typename P::Params p, c
   constexpr bool BWD = P::kBackward;
   constexpr unsigned FULL = 0xffffffffu;
   const int lane = threadIdx.x & 31;
+  // The carry composition (a programmatic dependent) may launch once every
+  // block of this one-wave grid is running; it waits for the grid to finish.
+  pdl_trigger();
   const int64_t sidx = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   if (sidx >= nseg) return;
   const int64_t s0 = sidx * L;

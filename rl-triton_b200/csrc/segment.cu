@@ -287,48 +287,72 @@ __device__ float vrow_decay(const SegArgs& a, int64_t i) {
   return decay_at(a, row, col);
 }
 
-// One block: the maps are staged in shared memory (coalesced), then warp 0
-// composes each lane's run serially, scans across the runs with shuffles and
-// re-walks its run, leaving the carries in place of the A's; all threads then
-// store them coalesced.
+// One block: each thread composes a run of up to six consecutive segments (in
+// walk order), the block scans the runs (warp shuffles, then the 32 warp
+// totals), and each thread re-walks its run from its exclusive prefix, storing
+// the carry entering every segment.  Launched as a programmatic dependent of
+// vseg_kernel: it starts while the scan drains and waits for it in pdl_wait.
 constexpr int kCarryThreads = 1024;
 __global__ void __launch_bounds__(kCarryThreads) vrows_carry(const float* seg_a, const float* seg_b, float* carry,
                                                              int64_t nseg, int backward) {
-  extern __shared__ float sm[];  // [nseg] a (then the carries), [nseg] b
-  float* sa = sm;
-  float* sb = sm + nseg;
-  for (int64_t i = threadIdx.x; i < nseg; i += kCarryThreads) {
-    sa[i] = seg_a[i];
-    sb[i] = seg_b[i];
+  __shared__ Pair s_warp[kCarryThreads / 32];
+  pdl_trigger();  // the fix-up may launch now; it waits for this grid in pdl_wait
+  pdl_wait();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t run = (nseg + kCarryThreads - 1) / kCarryThreads;
+  const int64_t w0 = threadIdx.x * run, w1 = (w0 + run < nseg) ? w0 + run : nseg;
+  auto seg_of = [&](int64_t w) { return backward ? nseg - 1 - w : w; };
+  Pair m = pair_identity();
+  for (int64_t w = w0; w < w1; ++w) {
+    const int64_t sg = seg_of(w);
+    m = compose(Pair{seg_a[sg], seg_b[sg]}, m);
   }
+  Pair incl = m;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const Pair o{__shfl_up_sync(0xffffffffu, incl.a, d), __shfl_up_sync(0xffffffffu, incl.b, d)};
+    if (lane >= d) incl = compose(incl, o);
+  }
+  if (lane == 31) s_warp[warp] = incl;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    const int64_t run = (nseg + 31) / 32;
-    const int64_t w0 = lane * run, w1 = (w0 + run < nseg) ? w0 + run : nseg;
-    auto seg_of = [&](int64_t w) { return backward ? nseg - 1 - w : w; };
-    Pair m = pair_identity();
-    for (int64_t w = w0; w < w1; ++w) {
-      const int64_t sg = seg_of(w);
-      m = compose(Pair{sa[sg], sb[sg]}, m);
-    }
-    Pair incl = m;
+  if (warp == 0) {
+    Pair x = s_warp[lane];
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
-      const Pair o{__shfl_up_sync(0xffffffffu, incl.a, d), __shfl_up_sync(0xffffffffu, incl.b, d)};
-      if (lane >= d) incl = compose(incl, o);
+      const Pair o{__shfl_up_sync(0xffffffffu, x.a, d), __shfl_up_sync(0xffffffffu, x.b, d)};
+      if (lane >= d) x = compose(x, o);
     }
-    float c = __shfl_up_sync(0xffffffffu, incl.a, 1);
-    if (lane == 0) c = 0.f;
-    for (int64_t w = w0; w < w1; ++w) {
-      const int64_t sg = seg_of(w);
-      const float next = fmaf(sb[sg], c, sa[sg]);
-      sa[sg] = c;  // now the carry entering segment sg
-      c = next;
-    }
+    s_warp[lane] = x;
   }
   __syncthreads();
-  for (int64_t i = threadIdx.x; i < nseg; i += kCarryThreads) carry[i] = sa[i];
+  Pair ex{__shfl_up_sync(0xffffffffu, incl.a, 1), __shfl_up_sync(0xffffffffu, incl.b, 1)};
+  if (lane == 0) ex = pair_identity();
+  if (warp > 0) ex = compose(ex, s_warp[warp - 1]);
+  float c = ex.a;  // the walk starts with carry 0
+  for (int64_t w = w0; w < w1; ++w) {
+    const int64_t sg = seg_of(w);
+    const float next = fmaf(seg_b[sg], c, seg_a[sg]);
+    carry[sg] = c;
+    c = next;
+  }
+}
+
+// Launch with programmatic stream serialization (the kernel calls pdl_wait()
+// before touching memory the preceding kernel writes).
+template <typename... KArgs, typename... Args>
+int launch_dependent(void (*kern)(KArgs...), unsigned blocks, unsigned threads, size_t smem, cudaStream_t s,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...) == cudaSuccess ? RLS_OK : RLS_ECUDA;
 }
 
 // Block per segment.  Code >= -1 (binary flags: b is 0 or coef): the decay
@@ -346,6 +370,7 @@ __global__ void __launch_bounds__(kBlockWalk) vrows_fixup(const SegArgs a, int64
   __shared__ float s_base;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t sg = blockIdx.x;
+  pdl_wait();
   const float c = carry[sg];
   const int code = seg_code[sg];
   __syncthreads();  // every thread has read its words before they are cleared
@@ -430,9 +455,128 @@ __global__ void __launch_bounds__(kBlockWalk) vrows_fixup(const SegArgs a, int64
   }
 }
 
+// V-trace virtual rows (kernels/vtrace_fused.py:98-196): each segment was
+// scanned with Delta = 0 entering at its far edge, so the true result adds
+// P[t] * c to the targets (P[t] = prod of b over t..far edge, b = gamma *
+// min(c_bar, ratio) * (1 - done), 0 at a row's last column) and
+// rho[t] * gamma * (1 - term[t]) * P[t+1] * c to the advantages where
+// vs_next is vs[t+1] (not truncated, not a row's last column).  One warp per
+// segment, 128 walk-order steps per pass (four per lane), until the product is
+// 0: the first reset, or underflow after a few hundred steps of c < 1.  Reads
+// lpt, lpb, term[, trunc] and both outputs only over that range.
+struct VtraceFixArgs {
+  const void *lpt, *lpb, *term, *trunc;
+  float *out0, *out1;
+  int bf16;
+  float gamma, rho_bar, c_bar;
+  int64_t M, S, L, nseg;
+};
+constexpr int kVfixElems = 8;
+// One pass of the walk for one lane: input loads and the per-step decay b and
+// advantage weight w of its kVfixElems steps.
+struct VfixPass {
+  float b[kVfixElems], w[kVfixElems];
+  int64_t idx[kVfixElems];
+  float mine;  // product of this lane's b
+};
+__device__ __forceinline__ void vfix_pass(const VtraceFixArgs& a, int64_t e, int64_t len, int64_t k0, int lane,
+                                          VfixPass& f) {
+  float lt[kVfixElems], lb[kVfixElems], tm[kVfixElems], tr[kVfixElems];
+#pragma unroll
+  for (int q = 0; q < kVfixElems; ++q) {
+    const int64_t k = k0 + (int64_t)lane * kVfixElems + q;
+    f.idx[q] = k < len ? e - 1 - k : -1;
+    const int64_t i = f.idx[q] >= 0 ? f.idx[q] : e - 1;
+    lt[q] = load_in(a.lpt, a.bf16, i);
+    lb[q] = load_in(a.lpb, a.bf16, i);
+    tm[q] = load_in(a.term, a.bf16, i);
+    tr[q] = a.trunc ? load_in(a.trunc, a.bf16, i) : 0.f;
+  }
+  f.mine = 1.f;
+#pragma unroll
+  for (int q = 0; q < kVfixElems; ++q) {
+    const bool row_end = f.idx[q] >= 0 && (f.idx[q] % a.S) == a.S - 1;
+    const float ratio = expf(lt[q] - lb[q]);
+    const float done = a.trunc ? fminf(tm[q] + tr[q], 1.f) : tm[q];
+    f.b[q] = f.idx[q] < 0 ? 1.f : (row_end ? 0.f : a.gamma * fminf(ratio, a.c_bar) * (1.f - done));
+    // weight of vs[t+1]'s correction in the advantage at t
+    f.w[q] = (f.idx[q] < 0 || row_end || tr[q] != 0.f) ? 0.f : fminf(ratio, a.rho_bar) * a.gamma * (1.f - tm[q]);
+    f.mine *= f.b[q];
+  }
+}
+
+// Launched as a programmatic dependent of vrows_carry (which triggers as soon
+// as it runs): the first pass's inputs -- which none of this call's kernels
+// write -- are loaded and turned into decays before pdl_wait, while the scan
+// and the carry composition finish; only the carry and the outputs are read
+// after it.
+__global__ void __launch_bounds__(128) vrows_fixup_vtrace(const VtraceFixArgs a, float* seg_a, float* seg_b,
+                                                          float* carry, int* seg_code) {
+  const int lane = threadIdx.x & 31;
+  const int64_t sg = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  const bool live = sg < a.nseg;
+  const int64_t s0 = live ? sg * a.L : 0;
+  const int64_t len = !live ? 0 : ((a.M - s0 < a.L) ? a.M - s0 : a.L);
+  const int64_t e = s0 + len;  // the carry enters here (walk runs e-1, e-2, ...)
+  VfixPass f;
+  if (live) vfix_pass(a, e, len, 0, lane, f);
+  pdl_wait();
+  if (!live) return;
+  const float c = carry[sg];
+  __syncwarp();  // every lane has read the carry before it is cleared
+  if (lane == 0) {
+    seg_a[sg] = 0.f;
+    seg_b[sg] = 0.f;
+    carry[sg] = 0.f;
+    seg_code[sg] = 0;
+  }
+  if (c == 0.f) return;  // uniform across the warp
+  float base = 1.f;      // product of b over all earlier walk steps
+  for (int64_t k0 = 0; k0 < len; k0 += 32 * kVfixElems) {
+    if (k0 > 0) vfix_pass(a, e, len, k0, lane, f);
+    float o0[kVfixElems], o1[kVfixElems];
+#pragma unroll
+    for (int q = 0; q < kVfixElems; ++q) {
+      const int64_t i = f.idx[q] >= 0 ? f.idx[q] : e - 1;
+      o0[q] = a.out0[i];
+      o1[q] = a.out1[i];
+    }
+    float incl = f.mine;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl *= o;
+    }
+    const float excl = __shfl_up_sync(0xffffffffu, incl, 1);
+    float P = base * (lane == 0 ? 1.f : excl);  // product over the walk steps before this lane's first
+#pragma unroll
+    for (int q = 0; q < kVfixElems; ++q) {
+      if (f.idx[q] < 0 || P == 0.f) break;
+      const int64_t i = f.idx[q];
+      if (f.w[q] != 0.f) a.out1[i] = fmaf(f.w[q] * P, c, o1[q]);
+      P *= f.b[q];
+      if (P != 0.f) a.out0[i] = fmaf(P, c, o0[q]);
+    }
+    base *= __shfl_sync(0xffffffffu, incl, 31);
+    if (base == 0.f) break;  // uniform
+  }
+}
+
 }  // namespace
 
 namespace rls {
+
+int vrows_finish_vtrace(const void* lpt, const void* lpb, const void* term, const void* trunc, int bf16, float* out0,
+                        float* out1, int64_t M, int64_t S, float gamma, float rho_bar, float c_bar, float* seg_a,
+                        float* seg_b, float* carry, int* seg_code, int64_t nseg, int64_t L, cudaStream_t s) {
+  if (nseg > 6144) return RLS_EINVAL;  // callers keep nseg <= 6144
+  VtraceFixArgs a{lpt, lpb, term, trunc, out0, out1, bf16, gamma, rho_bar, c_bar, M, S, L, nseg};
+  if (int st = launch_dependent(vrows_carry, 1, kCarryThreads, 0, s, (const float*)seg_a, (const float*)seg_b, carry,
+                                nseg, 1))
+    return st;
+  return launch_dependent(vrows_fixup_vtrace, (unsigned)((nseg + 3) / 4), 128, 0, s, a, seg_a, seg_b, carry,
+                          seg_code);
+}
 
 int vrows_finish(int alg, const void* f0, const void* f1, int bf16, float* out, int64_t M, int64_t S, float coef,
                  int ends_at, float* seg_a, float* seg_b, float* carry, int* seg_code, int64_t nseg, int64_t L,
@@ -449,11 +593,11 @@ int vrows_finish(int alg, const void* f0, const void* f1, int bf16, float* out, 
   a.ends_at = ends_at;
   a.halo = nullptr;
   a.backward = !(alg == RLS_ALG_ELIGIBILITY || alg == RLS_ALG_PREFIX || alg == RLS_ALG_SCAN_FWD);
-  const size_t smem = (size_t)nseg * 2 * sizeof(float);
-  if (smem > 48 * 1024) return RLS_EINVAL;  // callers keep nseg <= 6144
-  vrows_carry<<<1, kCarryThreads, smem, s>>>(seg_a, seg_b, carry, nseg, a.backward);
-  vrows_fixup<<<(unsigned)nseg, kBlockWalk, 0, s>>>(a, L, seg_a, seg_b, carry, seg_code);
-  return cudaPeekAtLastError() == cudaSuccess ? RLS_OK : RLS_ECUDA;
+  if (nseg > 6144) return RLS_EINVAL;  // callers keep nseg <= 6144
+  if (int st = launch_dependent(vrows_carry, 1, kCarryThreads, 0, s, (const float*)seg_a, (const float*)seg_b, carry,
+                                nseg, (int)a.backward))
+    return st;
+  return launch_dependent(vrows_fixup, (unsigned)nseg, kBlockWalk, 0, s, a, L, seg_a, seg_b, carry, seg_code);
 }
 
 }  // namespace rls

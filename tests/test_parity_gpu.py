@@ -137,6 +137,41 @@ def test_vtrace_random(n, t, mode):
     close(adv.cpu().numpy(), wadv, msg="advantages")
 
 
+@pytest.mark.parametrize("n,t", [(1, 300001), (64, 20000)])
+@pytest.mark.parametrize("regime", ["no_resets", "trunc_boot"])
+def test_vtrace_long_walks(n, t, regime, kernel_path):
+    """Few long rows with no episode resets and c = c_bar everywhere (target
+    log-probs above the behaviour ones): on the virtual-row path the carry
+    fix-up walks until gamma^k underflows, the longest walk it can take."""
+    import rl_triton
+    if kernel_path not in ("auto", "vrows", "flat3"):
+        pytest.skip("long-row families only")
+    g = np.random.default_rng(n + t)
+    lpb = (-g.random((n, t))).astype(np.float32)
+    lpt = (lpb + 0.1 + 0.2 * g.random((n, t))).astype(np.float32)
+    v = g.standard_normal((n, t)).astype(np.float32)
+    r = g.standard_normal((n, t)).astype(np.float32)
+    term = np.zeros((n, t), np.float32)
+    kw = dict(gamma=0.99, rho_bar=1.0, c_bar=1.0)
+    trunc = boot = None
+    kind = orc.BOOT_NONE
+    if regime == "trunc_boot":
+        trunc = (g.random((n, t)) < 1e-4).astype(np.float32)
+        boot = np.where(trunc == 1, g.standard_normal((n, t)), 0).astype(np.float32)
+        kw["truncateds"], kw["bootstrap_values"] = T(trunc), T(boot)
+        kind = orc.BOOT_FULL_ADD
+    vs, adv = rl_triton.compute_vtrace(T(lpt), T(lpb), T(v), T(r), T(term), **kw)
+
+    def oracle(k):
+        return lambda pr: orc.vtrace(lpt, lpb, v, r, term, trunc, boot, kind, 0.99, 1.0, 1.0, precision=pr)[k]
+
+    # Targets reach ~10 here and the advantages subtract them back to O(1):
+    # the shared element-wise rule (fp32 oracle, fp64 oracle, or no less
+    # accurate than the fp32 loop) decides.
+    _no_less_accurate(vs.cpu().numpy(), oracle(0), f"targets {n}x{t} {regime}")
+    _no_less_accurate(adv.cpu().numpy(), oracle(1), f"advantages {n}x{t} {regime}")
+
+
 @pytest.mark.parametrize("n,t,A", [(1, 1, 4), (3, 7, 4), (5, 129, 4), (64, 512, 4), (4096, 128, 4), (2, 3000, 4),
                                    (1, 70001, 4), (4, 33, 1), (3, 50, 3), (2, 77, 7), (2, 40, 18), (1, 300, 80)])
 def test_retrace_random(n, t, A):
