@@ -750,7 +750,9 @@ def run_e2e(cfg, x0, dev, split, world, ksteps):
     cs, ks, ds = (torch.cuda.Stream(dev) for _ in range(3))
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_free = [torch.cuda.Event() for _ in range(2)]
+    ev_out = [torch.cuda.Event() for _ in range(2)]
     pinned = [None, None]
+    keep = [None, None]  # step k's outputs stay referenced until their copy-out has run
 
     def step(k):
         b = k % 2
@@ -762,6 +764,14 @@ def run_e2e(cfg, x0, dev, split, world, ksteps):
             ev_in[b].record(cs)
         with torch.cuda.stream(ks):
             ks.wait_event(ev_in[b])
+            if keep[b] is not None:
+                # Step k-2's outputs return to the allocator only once the
+                # kernel stream has waited for their copy-out: their memory is
+                # reused in stream order, with no cross-stream record (which
+                # makes the caching allocator fall back to fresh cudaMalloc
+                # calls, and those synchronise the device).
+                ks.wait_event(ev_out[b])
+                keep[b] = None
             res = []
             for f, c in make_calls(cfg, {**bufs[b], **const}, split).items():
                 res.extend(flat_outputs(f, c()).values())
@@ -772,7 +782,8 @@ def run_e2e(cfg, x0, dev, split, world, ksteps):
                 pinned[b] = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
             for o, r in zip(pinned[b], res):
                 o.copy_(r, non_blocking=True)
-                r.record_stream(ds)
+            ev_out[b].record(ds)
+        keep[b] = res
         return res
 
     for k in range(4):  # warm-up, allocates the pinned result buffers
