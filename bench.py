@@ -91,6 +91,9 @@ CONFIGS = {
                  desc="config 4: GAE + V-trace, num_envs=131072 seq_len=1024, bf16 inputs, fp32 out (per GPU)"),
     "cfg5a": dict(N=64, T=131072, trunc=False, bf16=False, funcs=["vtrace"], p_term=0.01,
                   desc="config 5a: V-trace num_envs=64 seq_len=131072 fp32"),
+    "large": dict(N=131072, T=1024, trunc=False, bf16=False, funcs=FUNCS, p_term=0.01,
+                  desc="all seven estimators, num_envs=131072 seq_len=1024 fp32 (the second shape of the "
+                       "per-function roofline target; distributions of config 2)"),
     "unaligned": dict(N=4096, T=131, trunc=False, bf16=False, funcs=FUNCS, p_term=0.01,
                       desc="all seven estimators, num_envs=4096 seq_len=131 fp32 (rows not 16-byte aligned)"),
     "cfg5b": dict(N=1, T=1 << 28, trunc=False, bf16=False, funcs=["prefix", "gae"], p_term=1e-4, split=True,

@@ -522,7 +522,18 @@ __global__ void __launch_bounds__(128) vrows_fixup_vtrace(const VtraceFixArgs a,
   if (live) vfix_pass(a, e, len, 0, lane, f);
   pdl_wait();
   if (!live) return;
+  // The carry and the first pass's outputs are loaded together (one round trip).
   const float c = carry[sg];
+  float o0[kVfixElems], o1[kVfixElems];
+  auto load_outs = [&]() {
+#pragma unroll
+    for (int q = 0; q < kVfixElems; ++q) {
+      const int64_t i = f.idx[q] >= 0 ? f.idx[q] : e - 1;
+      o0[q] = a.out0[i];
+      o1[q] = a.out1[i];
+    }
+  };
+  load_outs();
   __syncwarp();  // every lane has read the carry before it is cleared
   if (lane == 0) {
     seg_a[sg] = 0.f;
@@ -533,13 +544,9 @@ __global__ void __launch_bounds__(128) vrows_fixup_vtrace(const VtraceFixArgs a,
   if (c == 0.f) return;  // uniform across the warp
   float base = 1.f;      // product of b over all earlier walk steps
   for (int64_t k0 = 0; k0 < len; k0 += 32 * kVfixElems) {
-    if (k0 > 0) vfix_pass(a, e, len, k0, lane, f);
-    float o0[kVfixElems], o1[kVfixElems];
-#pragma unroll
-    for (int q = 0; q < kVfixElems; ++q) {
-      const int64_t i = f.idx[q] >= 0 ? f.idx[q] : e - 1;
-      o0[q] = a.out0[i];
-      o1[q] = a.out1[i];
+    if (k0 > 0) {
+      vfix_pass(a, e, len, k0, lane, f);
+      load_outs();
     }
     float incl = f.mine;
 #pragma unroll
