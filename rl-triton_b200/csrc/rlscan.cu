@@ -933,7 +933,7 @@ int rls_retrace(const float* action_probs_target, const float* action_probs_beha
     if (staged) return launch_tile<RetraceT<true>, 9>(p, g, ws, ws_bytes, s);
     return launch_tile<RetraceT<false>, 9>(p, g, ws, ws_bytes, s);
   }
-  if ((mode == 0 || mode == 1 || mode == 4) && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 2>(p, g, s);
+  if ((mode == 0 || mode == 1 || mode == 4) && use_rows<RetraceAlg>(g)) return launch_rows<RetraceAlg, 1>(p, g, s);
   // Staging: one warp span of pi and Qn rows plus actions, E and pi_a.
   int rounds = pick_rounds(g.M, 4, 2);
   auto per_warp = [&](int r) {
