@@ -468,7 +468,8 @@ namespace {
 // second pass, no look-back), then compose the carries and apply the bounded
 // fix-up out[t] += P[t] * carry (vrows_finish), which touches each segment
 // only up to its first reset (or until P underflows).  Auto picks it when the
-// segments reach 16K steps and four times the decay's underflow length.
+// segments reach 24K steps (unit decay) or 4K steps and three times the decay's
+// underflow length (decays below one); shorter ones take flat4.
 struct VrowsSpec {
   int alg;
   const void* f0;
@@ -528,11 +529,20 @@ struct VSpec<ForwardT<T, PREV>> {
 };
 
 constexpr int64_t kVrowsSegs = 32 * 148;  // segments if the occupancy query fails: 32 warps per SM
-constexpr int64_t kVrowsMinLen = 16384;   // auto: shortest segment worth its fix-up
-constexpr int64_t kVrowsMinLenVtrace = 1024;  // the same for V-trace (its fix-up reads the decay)
+// auto: shortest segments worth their fix-up (measured against flat3 / flat4 on
+// one row of 2^22 .. 2^27 steps at a 1e-4 reset rate).  A unit decay (prefix
+// sums) adds the carry up to each segment's first reset; a decay below one
+// also stops where the product underflows (kVrowsUnderflows x that length is
+// the minimum); V-trace's per-step c < 1 usually ends its walk within a few
+// hundred steps.
+constexpr int64_t kVrowsMinLen = 4096;
+constexpr int64_t kVrowsMinLenUnit = 24576;
+constexpr double kVrowsUnderflows = 3.0;
+constexpr int64_t kVrowsMinLenVtrace = 1024;
 
-// forced (RLS_PATH=vrows): any length; auto: only when segments reach
-// kVrowsMinLen.  Policies with other outputs fall back to flat3.
+// forced (RLS_PATH=vrows): any length; auto: only when segments reach the
+// minimum above, else flat4.  Policies without a virtual-row fix-up and decay
+// coefficients outside (0, 1] take flat3.
 template <class P>
 int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t wsb, cudaStream_t s, bool forced) {
   constexpr int64_t CH = 32 * (16 / (int)sizeof(typename P::InT));
@@ -571,16 +581,17 @@ int launch_vrows(const typename P::Params& p, const Geom& g, void* ws, size_t ws
     const int64_t nseg = (g.M + L - 1) / L;
     // auto: the fix-up reaches up to -110 / ln(coef) steps into a segment (the
     // decay product underflows there); keep that under a quarter of it.
-    int64_t min_len = kVrowsMinLen;
+    int64_t min_len = v.coef == 1.f ? kVrowsMinLenUnit : kVrowsMinLen;
     if (IsVtrace<P>::value) {
       // The fix-up walks to the first reset or until the product of the
       // per-step c < 1 underflows (a few hundred steps at c_bar = 1); even a
       // walk over a whole segment re-reads fewer bytes than the scan did.
       min_len = kVrowsMinLenVtrace;
     } else if (v.coef > 0.f && v.coef < 1.f) {
-      min_len = std::max(min_len, (int64_t)(4.0 * -110.0 / std::log((double)v.coef)));
+      min_len = std::max(min_len, (int64_t)(kVrowsUnderflows * -110.0 / std::log((double)v.coef)));
     }
-    if ((!forced && L < min_len) || L > 0x7fffffffLL) return Flat3L<P>::run(p, g, ws, wsb, s);
+    if (L > 0x7fffffffLL) return Flat3L<P>::run(p, g, ws, wsb, s);
+    if (!forced && L < min_len) return Flat4L<P>::run(p, g, ws, wsb, s);
     // The segment words live in the stream's workspace across three launches,
     // enqueued under the caller's launch lock.
     float* seg_a = reinterpret_cast<float*>(static_cast<char*>(ws) + 64);
