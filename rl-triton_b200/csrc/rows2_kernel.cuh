@@ -958,28 +958,27 @@ __global__ void __launch_bounds__(128) vseg_kernel(const typename P::Params p, c
   RowCursor cur;
   Pair M = pair_identity();
   float carry = 0.f;
-  Rows2Chunk<P, 1> a, b;
-  flat_load<P, 1, true>(p, g.M, cbase(0), lane, a);
+  // A ring of D chunks: the loads of the next D-1 chunks are in flight while
+  // one is scanned (three for policies of up to three input streams, whose
+  // chunks are small; two otherwise).
+  constexpr int D = P::kNS <= 3 ? 3 : 2;
+  Rows2Chunk<P, 1> buf[D];
+#pragma unroll
+  for (int u = 0; u < D - 1; ++u)
+    if (u < nch) flat_load<P, 1, true>(p, g.M, cbase(u), lane, buf[u]);
 #pragma unroll 1
-  for (int64_t k = 0; k < nch; k += 2) {
-    if (k + 1 < nch) flat_load<P, 1, true>(p, g.M, cbase(k + 1), lane, b);
-    {
+  for (int64_t k = 0; k < nch; k += D) {
+#pragma unroll
+    for (int u = 0; u < D; ++u) {
+      const int64_t kk = k + u;
+      if (kk >= nch) break;
+      if (kk + D - 1 < nch) flat_load<P, 1, true>(p, g.M, cbase(kk + D - 1), lane, buf[(u + D - 1) % D]);
       CS cs;
-      flat_chunk_setup<P, 1>(g, cbase(k), lane, k == 0, cur, cs);
-      nb = cs.pass1(p, g, lane, a, nb);
-      if (code == -1) first_zero(cs, cbase(k));
+      flat_chunk_setup<P, 1>(g, cbase(kk), lane, kk == 0, cur, cs);
+      nb = cs.pass1(p, g, lane, buf[u], nb);
+      if (code == -1) first_zero(cs, cbase(kk));
       M = compose(cs.aggregate(), M);
-      carry = cs.pass2(p, g, a, carry);
-    }
-    if (k + 1 >= nch) break;
-    if (k + 2 < nch) flat_load<P, 1, true>(p, g.M, cbase(k + 2), lane, a);
-    {
-      CS cs;
-      flat_chunk_setup<P, 1>(g, cbase(k + 1), lane, false, cur, cs);
-      nb = cs.pass1(p, g, lane, b, nb);
-      if (code == -1) first_zero(cs, cbase(k + 1));
-      M = compose(cs.aggregate(), M);
-      carry = cs.pass2(p, g, b, carry);
+      carry = cs.pass2(p, g, buf[u], carry);
     }
   }
   if (!__all_sync(FULL, binary)) code = -2;
