@@ -485,16 +485,20 @@ def time_function(calls, fname, stream, use_graph, min_reps=8, max_reps=1000, bu
         except Exception as e:  # noqa: BLE001
             g = None
             out["graph_error"] = f"{type(e).__name__}: {str(e)[:200]}"
+    # One warm replay, then three timed ones; the median is reported (a single
+    # replay right after capture occasionally ran at half speed).
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(3)]
     with torch.cuda.stream(stream):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         if g is not None:
             g.replay()
-            e0.record(stream)
-            g.replay()
-            e1.record(stream)
+            for e0, e1 in evs:
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
     stream.synchronize()
     if g is not None:
-        out["us_per_launch"] = round(e0.elapsed_time(e1) * 1e3 / reps, 3)
+        ts = sorted(e0.elapsed_time(e1) for e0, e1 in evs)
+        out["us_per_launch"] = round(ts[1] * 1e3 / reps, 3)
         out["launch"] = "graph"
     del g
     with torch.cuda.stream(stream):
